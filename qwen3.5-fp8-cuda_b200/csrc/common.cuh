@@ -1,0 +1,177 @@
+// Shared device helpers for the sm_100a decode-path kernels.
+//
+// Everything here is inline PTX or plain CUDA; nothing is taken from a
+// vendor library.  The kernels that wait on an mbarrier bound every wait by
+// wall time (globaltimer) and report a timeout through a device error word
+// instead of hanging: see qwen_err_set() / qwen_get_device_error().
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#ifndef QWEN_WAIT_TIMEOUT_NS
+#define QWEN_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate wait
+#endif
+
+namespace qwen {
+
+typedef __nv_bfloat16 bf16;
+
+// Error codes recorded in the device error word (first error wins).
+enum : unsigned {
+  ERR_NONE = 0,
+  ERR_TIMEOUT_FULL = 1,     // consumer gave up waiting for a bulk copy
+  ERR_TIMEOUT_EMPTY = 2,    // producer gave up waiting for a free stage
+  ERR_TIMEOUT_DRAIN = 3,    // producer gave up waiting for its own copies
+};
+
+// One error word per shared library (each library is a single translation
+// unit).  Kernels set it with atomicCAS; the host reads and clears it.
+__device__ unsigned int g_qwen_err;
+
+__device__ __forceinline__ void qwen_err_set(unsigned code) {
+  atomicCAS(&g_qwen_err, 0u, code);
+}
+
+// ---------------------------------------------------------------------------
+// Conversions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf2f(bf16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ bf16 f2bf(float v) { return __float2bfloat16(v); }
+__device__ __forceinline__ float bfround(float v) { return __bfloat162float(__float2bfloat16(v)); }
+
+// Two BF16 packed in a 32-bit word -> two floats (exact).
+__device__ __forceinline__ float2 bf2x_to_f2(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+// Two E4M3 bytes (low byte = element 0) -> f16x2 (exact: every E4M3 value is an f16).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  uint32_t out;
+  unsigned short in16 = (unsigned short)(two_bytes & 0xffffu);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(out) : "h"(in16));
+  return out;
+}
+
+__device__ __forceinline__ float2 h2u_to_f2(uint32_t h) {
+  __half2 v = *reinterpret_cast<__half2*>(&h);
+  return __half22float2(v);
+}
+
+// ---------------------------------------------------------------------------
+// Warp / block reductions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Named barrier over `nthreads` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory addressing, mbarriers and bulk async copies
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait until the phase with `parity` of mbarrier `bar` has completed.
+// Returns false after QWEN_WAIT_TIMEOUT_NS of wall time.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > QWEN_WAIT_TIMEOUT_NS) return false;
+  }
+}
+
+// L2 policy for data read exactly once per step (weights): evict first.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 1-D bulk copy global -> shared, completion counted on mbarrier `bar` (bytes).
+// Both addresses 16-byte aligned, bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL)
+// ---------------------------------------------------------------------------
+// Block until the grids this grid depends on have completed and flushed.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next grid on the stream to start launching.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Loads that bypass L1 allocation (streamed data read once).
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+  return r;
+}
+
+// BF16 orderable key: unsigned order equals value order; -0 maps to +0.
+__device__ __forceinline__ uint32_t bf16_orderable(uint32_t bits16) {
+  bits16 &= 0xffffu;
+  if ((bits16 & 0x7fffu) == 0) bits16 = 0;
+  return (bits16 & 0x8000u) ? (~bits16 & 0xffffu) : (bits16 | 0x8000u);
+}
+__device__ __forceinline__ unsigned long long argmax_key(bf16 v, uint32_t index) {
+  uint32_t bits = __bfloat16_as_ushort(v);
+  return ((unsigned long long)bf16_orderable(bits) << 32) | (unsigned long long)(0xffffffffu - index);
+}
+
+}  // namespace qwen

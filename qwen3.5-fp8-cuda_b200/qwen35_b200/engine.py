@@ -1,0 +1,238 @@
+"""Batch-1 greedy decode engine for the Qwen3.5 hybrid decoder on one B200.
+
+Replaces the per-layer Python/ctypes orchestration of
+``QwenEngineFP8Opt._decode_step`` / ``forward`` (main.py:1509-1604) with a fixed
+sequence of C-ABI launches that is captured once into a CUDA graph:
+
+    embed(token)                                               1 kernel
+    per layer (5 kernels each):
+      full:   RMSNorm+q/k/v GEMVs | norm+RoPE+KV write+attention+gate | o_proj+residual
+      linear: RMSNorm+in_proj GEMVs with conv1d/SiLU and gate epilogues
+              | delta rule + gated RMSNorm | out_proj+residual
+      both:   RMSNorm+gate/up+SiLU | down+residual
+    RMSNorm + LM head + greedy argmax (+ position increment)   1 kernel
+
+Kernels are chained with programmatic dependent launch, so each GEMV starts
+streaming its weights while the previous kernel finishes.  The token and the
+position live on the device: the graph reads the token written by the
+previous replay's argmax, so a greedy loop never leaves the GPU.
+
+PyTorch is used for device buffers, the stream and graph capture only.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from .ops import scale_mode
+
+P = ctypes.c_void_p
+
+
+def _p(t) -> P:
+    return P(0) if t is None else P(t.data_ptr())
+
+
+def rope_tables(max_pos: int, rotary_dim: int, theta: float):
+    """Partial-RoPE tables [max_pos, rotary_dim] FP32 (main.py:525-533), built on the CPU."""
+    inv = 1.0 / (theta ** (torch.arange(0, rotary_dim, 2).float() / rotary_dim))
+    pos = torch.arange(max_pos).float()
+    freqs = torch.outer(pos, inv)
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos().contiguous(), emb.sin().contiguous()
+
+
+class Qwen35DecodeEngine:
+    """Greedy batch-1 decoder over device-resident weights (see ``weights.py``)."""
+
+    def __init__(self, cfg, weights, max_seq: int = 4096, device="cuda", keep_logits: bool = False,
+                 attn_chunk: int | None = None):
+        self.cfg = cfg
+        self.w = weights
+        self.max_seq = int(max_seq)
+        self.device = torch.device(device)
+        self.keep_logits = keep_logits
+        self.lib = _lib.fused()
+        dev = self.device
+        H = cfg.hidden_size
+        bf, f32 = torch.bfloat16, torch.float32
+
+        def empty(n, dt=bf):
+            return torch.empty(n, dtype=dt, device=dev)
+
+        self.hidden = empty(H)
+        self.h2 = empty(H)
+        qd = cfg.num_attention_heads * cfg.head_dim
+        kvd = cfg.num_key_value_heads * cfg.head_dim
+        self.q_all = empty(2 * qd)
+        self.k_new = empty(kvd)
+        self.v_new = empty(kvd)
+        self.attn_out = empty(max(qd, cfg.linear_value_dim))
+        self.qkv_conv = empty(cfg.conv_dim)
+        self.z = empty(cfg.linear_value_dim)
+        self.g = empty(cfg.linear_num_value_heads, f32)
+        self.beta = empty(cfg.linear_num_value_heads)
+        self.silu = empty(cfg.intermediate_size)
+        self.logits = empty(cfg.vocab_size) if keep_logits else None
+        self.token = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.key = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.am_ws = torch.zeros(2, dtype=torch.int64, device=dev)
+        cos, sin = rope_tables(self.max_seq, cfg.rotary_dim, cfg.rope_theta)
+        self.cos, self.sin = cos.to(dev), sin.to(dev)
+
+        # Split-KV attention: chunk positions per CTA.
+        if attn_chunk is None:
+            nsplit = min(64, max(1, math.ceil(self.max_seq / 32)))
+            attn_chunk = math.ceil(self.max_seq / nsplit)
+        self.attn_chunk = int(attn_chunk)
+        self.attn_nsplit = math.ceil(self.max_seq / self.attn_chunk)
+        self.attn_ws = empty(cfg.num_attention_heads * self.attn_nsplit * (cfg.head_dim + 2), f32)
+        self.attn_cnt = torch.zeros(cfg.num_key_value_heads, dtype=torch.int32, device=dev)
+
+        self.k_cache, self.v_cache, self.conv_state, self.state = {}, {}, {}, {}
+        for i, lt in enumerate(cfg.layer_types):
+            if lt == "full_attention":
+                shape = (cfg.num_key_value_heads, self.max_seq, cfg.head_dim)
+                self.k_cache[i] = torch.zeros(shape, dtype=bf, device=dev)
+                self.v_cache[i] = torch.zeros(shape, dtype=bf, device=dev)
+            else:
+                self.conv_state[i] = torch.zeros(cfg.conv_dim, cfg.linear_conv_kernel_dim, dtype=bf, device=dev)
+                self.state[i] = torch.zeros(cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                                            cfg.linear_value_head_dim, dtype=f32, device=dev)
+        self.graph = None
+        self._h_tok = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+        self._h_out = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+        self.launches_per_step = 0
+
+    # ------------------------------------------------------------------
+    def reset(self):
+        """Clear caches and recurrent state; position back to 0."""
+        for t in list(self.k_cache.values()) + list(self.v_cache.values()):
+            t.zero_()
+        for t in list(self.conv_state.values()) + list(self.state.values()):
+            t.zero_()
+        self.pos.zero_()
+
+    def _launch_step(self, stream):
+        cfg, lib, w = self.cfg, self.lib, self.w
+        H, I = cfg.hidden_size, cfg.intermediate_size
+        eps = cfg.rms_norm_eps
+        st = P(stream)
+        n = 0
+
+        def chk(status, what):
+            _lib.check(status, what)
+
+        chk(lib.qwen_embed(_p(w["embed"]), _p(self.token), _p(self.hidden), H, st), "qwen_embed")
+        n += 1
+        for i, ly in enumerate(w["layers"]):
+            if cfg.layer_types[i] == "full_attention":
+                (wq, sq), (wk, sk), (wv, sv), (wo, so) = ly["q_proj"], ly["k_proj"], ly["v_proj"], ly["o_proj"]
+                chk(lib.qwen_attn_in_proj(_p(self.hidden), _p(ly["input_layernorm"]), eps,
+                                          _p(wq), _p(sq), wq.shape[0], _p(wk), _p(sk), wk.shape[0],
+                                          _p(wv), _p(sv), wv.shape[0], H, scale_mode(wq.shape[0], sq),
+                                          _p(self.q_all), _p(self.k_new), _p(self.v_new), st), "attn_in_proj")
+                chk(lib.qwen_attn_decode(_p(self.q_all), _p(self.k_new), _p(self.v_new), _p(ly["q_norm"]),
+                                         _p(ly["k_norm"]), _p(self.cos), _p(self.sin), _p(self.k_cache[i]),
+                                         _p(self.v_cache[i]), _p(self.pos), self.max_seq,
+                                         cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim,
+                                         cfg.rotary_dim, eps, self.attn_chunk, self.attn_nsplit,
+                                         _p(self.attn_ws), _p(self.attn_cnt), _p(self.attn_out), st), "attn_decode")
+                chk(lib.qwen_linear_resid(_p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1],
+                                          scale_mode(wo.shape[0], so), _p(self.hidden), _p(self.h2), st), "o_proj")
+            else:
+                (wqkv, sqkv), (wz, sz) = ly["in_proj_qkv"], ly["in_proj_z"]
+                (wa, sa), (wb, sb), (wo, so) = ly["in_proj_a"], ly["in_proj_b"], ly["out_proj"]
+                chk(lib.qwen_gdn_in_proj(_p(self.hidden), _p(ly["input_layernorm"]), eps, H,
+                                         scale_mode(wqkv.shape[0], sqkv), _p(wqkv), _p(sqkv), wqkv.shape[0],
+                                         _p(ly["conv1d_w"]), _p(self.conv_state[i]), cfg.linear_conv_kernel_dim,
+                                         _p(self.qkv_conv), _p(wz), _p(sz), wz.shape[0], _p(self.z),
+                                         _p(wa), _p(sa), _p(wb), _p(sb), wa.shape[0], _p(ly["A_log"]),
+                                         _p(ly["dt_bias"]), _p(self.g), _p(self.beta), st), "gdn_in_proj")
+                chk(lib.qwen_gdn_decode(_p(self.qkv_conv), _p(self.g), _p(self.beta), _p(self.state[i]),
+                                        _p(self.z), _p(ly["norm_w"]), eps, _p(self.attn_out),
+                                        cfg.linear_num_key_heads, cfg.linear_num_value_heads,
+                                        cfg.linear_value_head_dim, st), "gdn_decode")
+                chk(lib.qwen_linear_resid(_p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1],
+                                          scale_mode(wo.shape[0], so), _p(self.hidden), _p(self.h2), st),
+                    "out_proj")
+            (wg, sg), (wu, su), (wd, sd) = ly["gate_proj"], ly["up_proj"], ly["down_proj"]
+            chk(lib.qwen_mlp_gate_up(_p(self.h2), _p(ly["post_attention_layernorm"]), eps, _p(wg), _p(sg),
+                                     _p(wu), _p(su), I, H, scale_mode(I, sg), _p(self.silu), st), "gate_up")
+            chk(lib.qwen_linear_resid(_p(self.silu), _p(wd), _p(sd), H, I, scale_mode(H, sd), _p(self.h2),
+                                      _p(self.hidden), st), "down")
+            n += 5
+        head = w["lm_head"]
+        if not isinstance(head, tuple):
+            raise NotImplementedError("BF16 LM head: use an FP8 head (cfg.fp8_lm_head=True)")
+        wh, sh = head
+        chk(lib.launch_lm_head_argmax(_p(self.hidden), _p(w["norm_f"]), eps, _p(wh), _p(sh), wh.shape[0], H,
+                                      scale_mode(wh.shape[0], sh), 0, _p(self.am_ws), _p(self.key), _p(self.token),
+                                      _p(self.logits), _p(self.pos), st), "lm_head_argmax")
+        n += 1
+        self.launches_per_step = n
+
+    # ------------------------------------------------------------------
+    def step_eager(self):
+        """Run one decode step without the graph (token and pos on device)."""
+        self._launch_step(torch.cuda.current_stream().cuda_stream)
+
+    def capture(self):
+        """Capture one decode step into a CUDA graph (state is not advanced)."""
+        saved = [t.clone() for t in self._mutable()]
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._launch_step(s.cuda_stream)  # warm-up (sets kernel attributes)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self._launch_step(s.cuda_stream)
+        torch.cuda.synchronize(self.device)
+        for t, v in zip(self._mutable(), saved):
+            t.copy_(v)
+        self.graph = g
+        return g
+
+    def _mutable(self):
+        return ([self.token, self.key, self.pos, self.hidden, self.h2] + list(self.k_cache.values())
+                + list(self.v_cache.values()) + list(self.conv_state.values()) + list(self.state.values()))
+
+    def step(self):
+        """One decode step on the device (graph replay if captured)."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.step_eager()
+
+    # ------------------------------------------------------------------
+    # Public API: host token in, host token out (one step end to end).
+    def decode(self, token: int) -> int:
+        """Feed ``token`` at the current position; return the greedy next token."""
+        self._h_tok[0] = int(token)
+        self.token.copy_(self._h_tok, non_blocking=True)
+        self.step()
+        self._h_out.copy_(self.token, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return int(self._h_out[0])
+
+    def generate(self, prompt, n_new: int):
+        """Greedy generation: feed the prompt token by token, then ``n_new`` steps on device."""
+        out = []
+        nxt = None
+        for t in prompt:
+            nxt = self.decode(int(t))
+        tok = nxt
+        for _ in range(n_new):
+            out.append(tok)
+            tok = self.decode(tok)
+        return out, tok
+
+    def position(self) -> int:
+        return int(self.pos.item())

@@ -1,0 +1,191 @@
+"""GPU parity of the GatedDeltaNet decode path: the reference-named delta-rule,
+gate and gated-norm entry points, the 300-step state drift bar, and the
+engine's fused in_proj (conv1d + gates) / decode kernels on a full-size layer."""
+
+import ctypes
+import math
+import os
+
+import pytest
+import torch
+
+from conftest import REF_LIB
+from oracle import ops, synth
+from parity import assert_close, bf16_ulp_diff, max_rel
+
+pytestmark = pytest.mark.gpu
+
+P = ctypes.c_void_p
+BF16, F32 = torch.bfloat16, torch.float32
+HV, HK, D = 32, 16, 128
+
+
+def _p(t):
+    return P(0) if t is None else P(t.data_ptr())
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from qwen35_b200 import _lib
+    return _lib.fused()
+
+
+def step_inputs(g, heads=HV):
+    q = torch.randn(heads, D, generator=g).to(BF16)
+    k = torch.randn(heads, D, generator=g).to(BF16)
+    v = (torch.randn(heads, D, generator=g) * 3).to(BF16)
+    gg = -torch.rand(heads, generator=g) * 2.0
+    beta = torch.rand(heads, generator=g).to(BF16)
+    return q, k, v, gg, beta
+
+
+def run_delta(lib, q, k, v, gg, beta, state_dev):
+    out = torch.empty(q.shape, dtype=BF16, device="cuda")
+    dq, dk, dv, dg, db = (t.cuda() for t in (q, k, v, gg, beta))
+    lib.launch_delta_rule_decode(_p(dq), _p(dk), _p(dv), _p(dg), _p(db), _p(state_dev), _p(out), q.shape[0], D, P(0))
+    assert lib.qwen_last_error() == 0
+    return out
+
+
+def test_delta_rule_single_step(lib):
+    g = synth.gen(3)
+    q, k, v, gg, beta = step_inputs(g)
+    s0 = torch.randn(HV, D, D, generator=g) * 0.1
+    sd = s0.cuda()
+    out = run_delta(lib, q, k, v, gg, beta, sd)
+    torch.cuda.synchronize()
+    o_ref, s_ref = ops.delta_rule_decode(q, k, v, gg, beta, s0)
+    assert max_rel(sd, s_ref) < 1e-5
+    assert max_rel(out, o_ref) < 4e-3
+
+
+def test_delta_rule_state_after_300_steps(lib):
+    """The contract bar: FP32 state within 1e-3 relative after 300 steps."""
+    g = synth.gen(4)
+    s_ref = torch.zeros(HV, D, D)
+    sd = torch.zeros(HV, D, D, device="cuda")
+    worst_out = 0.0
+    for _ in range(300):
+        q, k, v, gg, beta = step_inputs(g)
+        out = run_delta(lib, q, k, v, gg, beta, sd)
+        o_ref, s_ref = ops.delta_rule_decode(q, k, v, gg, beta, s_ref)
+        worst_out = max(worst_out, max_rel(out, o_ref))
+    torch.cuda.synchronize()
+    err = max_rel(sd, s_ref)
+    assert err < 1e-3, err
+    assert worst_out < 4e-3
+
+
+def test_gates_and_gated_norm_reference_kernels(lib):
+    g = synth.gen(5)
+    a = (torch.randn(HV, generator=g) * 8).to(BF16)
+    a[0] = 30.0  # softplus above its threshold
+    b = (torch.randn(HV, generator=g) * 3).to(BF16)
+    a_log = torch.log(torch.rand(HV, generator=g) * 15 + 1)
+    dt = torch.ones(HV)
+    g_out = torch.empty(HV, dtype=F32, device="cuda")
+    b_out = torch.empty(HV, dtype=BF16, device="cuda")
+    lib.launch_prepare_linear_gates(_p(a.cuda()), _p(b.cuda()), _p(a_log.cuda()), _p(dt.cuda()), _p(g_out),
+                                    _p(b_out), HV, P(0))
+    core = (torch.randn(HV, D, generator=g) * 2).to(BF16)
+    z = (torch.randn(HV, D, generator=g) * 2).to(BF16)
+    w = (1 + torch.randn(D, generator=g) * 0.02).to(BF16)
+    out = torch.empty(HV, D, dtype=BF16, device="cuda")
+    lib.launch_rmsnorm_gated_decode(_p(core.cuda()), _p(z.cuda()), _p(w.cuda()), _p(out), HV, D, 1e-6, P(0))
+    assert lib.qwen_last_error() == 0
+    torch.cuda.synchronize()
+    g_ref, b_ref = ops.linear_gates(a, b, a_log, dt)
+    assert max_rel(g_out, g_ref) < 1e-5
+    assert torch.equal(b_out.cpu(), b_ref)
+    cf = core.float()
+    ref32 = cf * torch.rsqrt((cf * cf).mean(-1, keepdim=True) + 1e-6) * w.float() * ops.silu_f32(z.float())
+    assert_close(out.cpu(), ref32, what="gated norm (fp32 form)")
+
+
+def test_gdn_layer_engine_kernels(lib):
+    """qwen_gdn_in_proj + qwen_gdn_decode + qwen_linear_resid on a full-size
+    GDN layer against oracle.model's layer (main.py:1064-1163 semantics)."""
+    from qwen35_b200.config import qwen35_4b
+    cfg = qwen35_4b()
+    g = synth.gen(6)
+    Hh = cfg.hidden_size
+    conv_dim, vd = cfg.conv_dim, cfg.linear_value_dim
+    mats = {"qkv": synth.fp8_weight(conv_dim, Hh, g), "z": synth.fp8_weight(vd, Hh, g),
+            "a": synth.fp8_weight(HV, Hh, g), "b": synth.fp8_weight(HV, Hh, g), "out": synth.fp8_weight(Hh, vd, g)}
+    mats = {k: (w, s.to(BF16)) for k, (w, s) in mats.items()}
+    ln = torch.randn(Hh, generator=g) * 0.02
+    conv_w = (torch.randn(conv_dim, 4, generator=g) * 0.1).to(BF16)
+    conv_state = (torch.randn(conv_dim, 4, generator=g)).to(BF16)
+    a_log = torch.log(torch.rand(HV, generator=g) * 15 + 1)
+    dt = torch.ones(HV)
+    norm_w = (1 + torch.randn(D, generator=g) * 0.02).to(BF16)
+    state = torch.randn(HV, D, D, generator=g) * 0.05
+    hidden = (torch.randn(Hh, generator=g) * 2).to(BF16)
+
+    # oracle
+    h = ops.rmsnorm(hidden, ln)
+    mixed = ops.gemv(h, *mats["qkv"])
+    z = ops.gemv(h, *mats["z"])
+    a = ops.gemv(h, *mats["a"])
+    b = ops.gemv(h, *mats["b"])
+    conv_out, conv_ref = ops.conv1d_update(mixed, conv_state, conv_w)
+    kd = cfg.linear_key_dim
+    q, k, v = torch.split(conv_out, [kd, kd, vd])
+    gg, beta = ops.linear_gates(a, b, a_log, dt)
+    qr = q.reshape(HK, D).repeat_interleave(2, 0)
+    kr = k.reshape(HK, D).repeat_interleave(2, 0)
+    core, s_ref = ops.delta_rule_decode(qr, kr, v.reshape(HV, D), gg, beta, state)
+    gated = ops.rmsnorm_gated(core, z.reshape(HV, D), norm_w)
+    y_ref32 = hidden.float() + (ops.dequant(*mats["out"]) @ gated.reshape(-1).float()).to(BF16).float()
+
+    dev = {k: (w.cuda(), s.cuda()) for k, (w, s) in mats.items()}
+    qkv_out = torch.empty(conv_dim, dtype=BF16, device="cuda")
+    z_out = torch.empty(vd, dtype=BF16, device="cuda")
+    g_out = torch.empty(HV, dtype=F32, device="cuda")
+    b_out = torch.empty(HV, dtype=BF16, device="cuda")
+    cs = conv_state.cuda()
+    sd = state.cuda()
+    gated_out = torch.empty(vd, dtype=BF16, device="cuda")
+    y = torch.empty(Hh, dtype=BF16, device="cuda")
+    dh = hidden.cuda()
+    st = lib.qwen_gdn_in_proj(_p(dh), _p(ln.cuda()), 1e-6, Hh, 20, _p(dev["qkv"][0]), _p(dev["qkv"][1]), conv_dim,
+                              _p(conv_w.cuda()), _p(cs), 4, _p(qkv_out), _p(dev["z"][0]), _p(dev["z"][1]), vd,
+                              _p(z_out), _p(dev["a"][0]), _p(dev["a"][1]), _p(dev["b"][0]), _p(dev["b"][1]), HV,
+                              _p(a_log.cuda()), _p(dt.cuda()), _p(g_out), _p(b_out), P(0))
+    assert st == 0
+    st = lib.qwen_gdn_decode(_p(qkv_out), _p(g_out), _p(b_out), _p(sd), _p(z_out), _p(norm_w.cuda()), 1e-6,
+                             _p(gated_out), HK, HV, D, P(0))
+    assert st == 0
+    st = lib.qwen_linear_resid(_p(gated_out), _p(dev["out"][0]), _p(dev["out"][1]), Hh, vd, 32, _p(dh), _p(y), P(0))
+    assert st == 0
+    torch.cuda.synchronize()
+    # stage by stage against the oracle
+    assert max_rel(qkv_out, conv_out) < 4e-3
+    assert max_rel(cs, conv_ref) < 4e-3
+    assert max_rel(z_out, z) < 4e-3
+    assert max_rel(g_out, gg) < 2e-3
+    assert float(bf16_ulp_diff(b_out, beta).max()) <= 1.0
+    assert max_rel(sd, s_ref) < 5e-3
+    assert_close(y.cpu(), y_ref32, max_rel_err=4e-3, min_cos=0.9999, what="gdn layer out")
+    from qwen35_b200 import _lib
+    assert _lib.device_error() == 0
+
+
+def test_against_reference_delta_kernel(lib):
+    path = os.path.join(REF_LIB, "libref_fused.so")
+    if not os.path.exists(path):
+        pytest.skip("reference kernels not built")
+    ref = ctypes.CDLL(path)
+    ref.launch_delta_rule_decode.argtypes = [P] * 7 + [ctypes.c_int, ctypes.c_int, P]
+    g = synth.gen(9)
+    q, k, v, gg, beta = step_inputs(g)
+    s0 = torch.randn(HV, D, D, generator=g) * 0.1
+    s_ours, s_refk = s0.cuda(), s0.cuda()
+    out = run_delta(lib, q, k, v, gg, beta, s_ours)
+    out_r = torch.empty(HV, D, dtype=BF16, device="cuda")
+    dq, dk, dv, dg, db = (t.cuda() for t in (q, k, v, gg, beta))
+    ref.launch_delta_rule_decode(_p(dq), _p(dk), _p(dv), _p(dg), _p(db), _p(s_refk), _p(out_r), HV, D, P(0))
+    torch.cuda.synchronize()
+    assert max_rel(s_ours, s_refk) < 1e-5
+    assert max_rel(out, out_r) < 4e-3
+    assert not math.isnan(float(out.float().sum()))

@@ -1,0 +1,231 @@
+"""GPU parity of the block-scaled E4M3 GEMV family against the CPU oracle.
+
+Covers BASELINE config 0 (9216x2560) and every GEMV shape of config 1, the
+three reference scale modes, FP32 scales, ragged / small shapes, the generic
+fallback kernel, the grouped (multi-segment) launches and the reference's own
+kernels compiled for sm_100a (oracle/_ref) on the same inputs.
+"""
+
+import ctypes
+import os
+
+import pytest
+import torch
+
+from conftest import REF_LIB
+from oracle import ops, synth
+from parity import assert_close, bf16_ulp_diff
+
+pytestmark = pytest.mark.gpu
+
+P = ctypes.c_void_p
+BF16 = torch.bfloat16
+
+
+def _p(t):
+    return P(0) if t is None else P(t.data_ptr())
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from qwen35_b200 import _lib
+    return _lib.fused()
+
+
+def run_gemv(lib, x, w, s, kblk, f32=False):
+    n, k = w.shape
+    y = torch.empty(n, dtype=BF16, device="cuda")
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()
+    if f32:
+        assert lib.launch_gemv_f32s(_p(xd), _p(wd), _p(sd), _p(y), n, k, kblk, P(0)) == 0
+    else:
+        lib.launch_gemv_v4_extern(_p(xd), _p(wd), _p(sd), _p(y), n, k, kblk, P(0))
+        assert lib.qwen_last_error() == 0
+    torch.cuda.synchronize()
+    return y.cpu()
+
+
+def oracle_f32(x, w, s, kblk):
+    return ops.dequant(w, s, kblk) @ x.float()
+
+
+def test_config0_gemv(lib):
+    x, w, s32 = synth.config0(seed=0)
+    s = s32.to(BF16)  # the ABI path consumes BF16 scales (main.py:597)
+    y = run_gemv(lib, x, w, s, ops.scale_mode(9216, s))
+    ref = oracle_f32(x, w, s, 20)
+    assert_close(y, ref, what="config0")
+    # against the oracle's own BF16 output: almost all elements identical
+    assert float((bf16_ulp_diff(y, ref.to(BF16)) > 0).float().mean()) < 0.01
+
+
+@pytest.mark.parametrize("name,n,k", synth.LAYER_GEMVS)
+def test_config1_layer_shapes(lib, name, n, k):
+    g = synth.gen(hash(name) % 1000)
+    x = synth.bf16_vector(k, g)
+    w, s32 = synth.fp8_weight(n, k, g)
+    s = s32.to(BF16)
+    kblk = ops.scale_mode(n, s)
+    y = run_gemv(lib, x, w, s, kblk)
+    assert_close(y, oracle_f32(x, w, s, kblk), what=name)
+
+
+@pytest.mark.parametrize("mode", ["per_row", "per_row_block"])
+def test_scale_modes(lib, mode):
+    g = synth.gen(7)
+    n, k = 1024, 2560
+    x = synth.bf16_vector(k, g)
+    w, _ = synth.fp8_weight(n, k, g)
+    if mode == "per_row":
+        s = torch.pow(10.0, torch.rand(n, 1, generator=g) * 2 - 4).to(BF16)
+    else:
+        s = torch.pow(10.0, torch.rand(n, k // 128, generator=g) * 2 - 4).to(BF16)
+    kblk = ops.scale_mode(n, s)
+    assert kblk == (1 if mode == "per_row" else -(k // 128))
+    y = run_gemv(lib, x, w, s, kblk)
+    assert_close(y, oracle_f32(x, w, s, kblk), what=mode)
+
+
+def test_f32_scales(lib):
+    x, w, s32 = synth.config0(seed=3)
+    y = run_gemv(lib, x, w, s32, 20, f32=True)
+    assert_close(y, oracle_f32(x, w, s32, 20), what="f32 scales")
+
+
+@pytest.mark.parametrize("n,k", [(1, 512), (31, 2560), (32, 2560), (129, 4096), (1000, 9216), (300, 256),
+                                 (257, 384), (77, 1280), (513, 6144)])
+def test_ragged_shapes(lib, n, k):
+    g = synth.gen(n * 7 + k)
+    x = synth.bf16_vector(k, g)
+    w, s32 = synth.fp8_weight(n, k, g)
+    s = s32.to(BF16)
+    kblk = ops.scale_mode(n, s)
+    y = run_gemv(lib, x, w, s, kblk)
+    assert_close(y, oracle_f32(x, w, s, kblk), what=f"{n}x{k}")
+
+
+@pytest.mark.parametrize("n,k", [(9216, 2560), (2560, 9216), (2560, 4096)])
+def test_generic_fallback_kernel(lib, n, k):
+    g = synth.gen(11)
+    x = synth.bf16_vector(k, g)
+    w, s32 = synth.fp8_weight(n, k, g)
+    s = s32.to(BF16)
+    y = torch.empty(n, dtype=BF16, device="cuda")
+    assert lib.qwen_gemv_generic(_p(x.cuda()), _p(w.cuda()), _p(s.cuda()), 0, _p(y), n, k, k // 128, P(0)) == 0
+    torch.cuda.synchronize()
+    assert_close(y.cpu(), oracle_f32(x, w, s, k // 128), what="generic")
+
+
+def test_extreme_values(lib):
+    """Subnormal / max-magnitude E4M3 codes, zero and large x blocks."""
+    n, k = 256, 2560
+    codes = torch.arange(256, dtype=torch.int32)
+    finite = codes[(codes & 0x7F) != 0x7F].to(torch.uint8)  # drop the two NaN codes
+    w = finite[torch.randint(0, finite.numel(), (n, k), generator=synth.gen(5))].contiguous()
+    x = torch.randn(k, generator=synth.gen(6))
+    x[:128] = 0.0                      # an all-zero K block
+    x[128:256] *= 1e4                  # a large block
+    x[256:384] *= 1e-6                 # a tiny block
+    x = x.to(BF16)
+    s = torch.pow(10.0, torch.rand(2, 20, generator=synth.gen(8)) * 2 - 4).to(BF16)
+    y = run_gemv(lib, x, w, s, 20)
+    assert_close(y, oracle_f32(x, w, s, 20), what="extremes")
+
+
+def test_grouped_in_proj4(lib):
+    """launch_linear_in_proj4 with the GDN in_proj shapes (main.py:1379-1389)."""
+    g = synth.gen(21)
+    k = 2560
+    x = synth.bf16_vector(k, g)
+    shapes = [8192, 32, 32, 4096]
+    ws = [synth.fp8_weight(n, k, g) for n in shapes]
+    ws = [(w, s.to(BF16)) for w, s in ws]
+    ys = [torch.empty(n, dtype=BF16, device="cuda") for n in shapes]
+    args = [_p(x.cuda())]
+    dev = [(w.cuda(), s.cuda()) for w, s in ws]
+    for (w, s), y, n in zip(dev, ys, shapes):
+        args += [_p(w), _p(s), _p(y), n, ops.scale_mode(n, s)]
+    lib.launch_linear_in_proj4(*args, k, P(0))
+    assert lib.qwen_last_error() == 0
+    torch.cuda.synchronize()
+    for (w, s), y, n in zip(ws, ys, shapes):
+        assert_close(y.cpu(), oracle_f32(x, w, s, ops.scale_mode(n, s)), what=f"in_proj4 n={n}")
+
+
+def test_fused_qkv_and_gate_up_wrappers():
+    from qwen35_b200 import ops as qops
+    g = synth.gen(31)
+    k = 2560
+    x = synth.bf16_vector(k, g)
+    mats = {n: synth.fp8_weight(n, k, g) for n in (8192, 1024, 1025)}
+    mats = {n: (w, s.to(BF16)) for n, (w, s) in mats.items()}
+    (wq, sq), (wk, sk), (wv, sv) = mats[8192], mats[1024], mats[1025]
+    dq = [t.cuda() for t in (wq, sq, wk, sk, wv, sv)]
+    q, kk, v = qops.fused_qkv(x.cuda(), *dq)
+    torch.cuda.synchronize()
+    assert_close(q.cpu(), oracle_f32(x, wq, sq, 20), what="q")
+    assert_close(kk.cpu(), oracle_f32(x, wk, sk, 20), what="k")
+    assert_close(v.cpu(), oracle_f32(x, wv, sv, 20), what="v")
+    gate, up = qops.fused_gate_up(x.cuda(), dq[0], dq[1], dq[2], dq[3])
+    torch.cuda.synchronize()
+    assert_close(gate.cpu(), oracle_f32(x, wq, sq, 20), what="gate")
+    assert_close(up.cpu(), oracle_f32(x, wk, sk, 20), what="up")
+
+
+def test_fp8_linear_dispatch():
+    """fp8_linear: M == 1 -> GEMV, M > 1 -> fp8_gemm_batch (main.py:242-270)."""
+    from qwen35_b200 import ops as qops
+    g = synth.gen(41)
+    n, k = 1024, 2560
+    w, s32 = synth.fp8_weight(n, k, g)
+    s = s32.to(BF16)
+    x = torch.randn(3, k, generator=g).to(BF16)
+    y = qops.fp8_linear(x.cuda(), w.cuda(), s.cuda())
+    torch.cuda.synchronize()
+    ref = x.float() @ ops.dequant(w, s).T
+    assert_close(y.cpu(), ref, what="gemm batch")
+    y1 = qops.fp8_linear(x[:1].cuda(), w.cuda(), s.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(y1.cpu()[0], y.cpu()[0])
+
+
+def test_invalid_arguments_launch_nothing(lib):
+    y = torch.full((16,), 7.0, dtype=BF16, device="cuda")
+    x = torch.zeros(24, dtype=BF16, device="cuda")
+    w = torch.zeros(16, 24, dtype=torch.uint8, device="cuda")
+    s = torch.ones(1, 1, dtype=BF16, device="cuda")
+    lib.launch_gemv_v4_extern(_p(x), _p(w), _p(s), _p(y), 16, 12, 1, P(0))  # K % 8 != 0
+    assert lib.qwen_last_error() != 0
+    lib.launch_gemv_v4_extern(_p(x), P(0), _p(s), _p(y), 16, 24, 1, P(0))  # null weight
+    assert lib.qwen_last_error() != 0
+    torch.cuda.synchronize()
+    assert bool((y.float() == 7.0).all())
+
+
+def _ref_lib():
+    path = os.path.join(REF_LIB, "libref_fused.so")
+    if not os.path.exists(path):
+        pytest.skip("reference kernels not built (oracle/Makefile)")
+    ref = ctypes.CDLL(path)
+    ref.launch_gemv_v4_extern.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
+    return ref
+
+
+@pytest.mark.parametrize("name,n,k", [("config0", 9216, 2560)] + synth.LAYER_GEMVS[:4])
+def test_against_reference_kernel(lib, name, n, k):
+    """Same inputs through the reference's gemv_v4_kernel built for sm_100a."""
+    ref = _ref_lib()
+    g = synth.gen(100 + n)
+    x = synth.bf16_vector(k, g)
+    w, s32 = synth.fp8_weight(n, k, g)
+    s = s32.to(BF16)
+    kblk = ops.scale_mode(n, s)
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()
+    yr = torch.empty(n, dtype=BF16, device="cuda")
+    ref.launch_gemv_v4_extern(_p(xd), _p(wd), _p(sd), _p(yr), n, k, kblk, P(0))
+    y = run_gemv(lib, x, w, s, kblk)
+    torch.cuda.synchronize()
+    o = oracle_f32(x, w, s, kblk)
+    assert_close(yr.cpu(), o, what="reference kernel vs oracle")
+    assert_close(y, o, what="ours vs oracle")
+    assert float((bf16_ulp_diff(y, yr.cpu()) > 1).float().mean()) < 0.001
