@@ -49,7 +49,13 @@ def main():
     fused.layer_mid_attn.argtypes = [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P]
     g = torch.Generator().manual_seed(4321)
     out = {}
-    c = lambda t: t.cuda().contiguous()  # noqa: E731
+    keep = []  # device copies must outlive the asynchronous launches that read them
+
+    def c(t):
+        d = t.cuda().contiguous()
+        keep.append(d)
+        return d
+
     p = lambda t: P(t.data_ptr())  # noqa: E731
 
     # GEMV in the three scale modes

@@ -111,7 +111,8 @@ def test_generic_fallback_kernel(lib, n, k):
     w, s32 = synth.fp8_weight(n, k, g)
     s = s32.to(BF16)
     y = torch.empty(n, dtype=BF16, device="cuda")
-    assert lib.qwen_gemv_generic(_p(x.cuda()), _p(w.cuda()), _p(s.cuda()), 0, _p(y), n, k, k // 128, P(0)) == 0
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()  # alive across the launch
+    assert lib.qwen_gemv_generic(_p(xd), _p(wd), _p(sd), 0, _p(y), n, k, k // 128, P(0)) == 0
     torch.cuda.synchronize()
     assert_close(y.cpu(), oracle_f32(x, w, s, k // 128), what="generic")
 
@@ -141,7 +142,8 @@ def test_grouped_in_proj4(lib):
     ws = [synth.fp8_weight(n, k, g) for n in shapes]
     ws = [(w, s.to(BF16)) for w, s in ws]
     ys = [torch.empty(n, dtype=BF16, device="cuda") for n in shapes]
-    args = [_p(x.cuda())]
+    xd = x.cuda()
+    args = [_p(xd)]
     dev = [(w.cuda(), s.cuda()) for w, s in ws]
     for (w, s), y, n in zip(dev, ys, shapes):
         args += [_p(w), _p(s), _p(y), n, ops.scale_mode(n, s)]

@@ -77,8 +77,8 @@ def test_layer_post_o_fp8_mlp(lib):
     assert_close(up.cpu(), u32, what="up")
     assert_close(silu.cpu(), ops.silu_f32(g32) * u32, what="silu*up")
     d32 = ops.dequant(wd, sd) @ silu.cpu().float()  # down of our own SiLU output
-    assert_close(ws.cpu(), d32, what="down")
-    assert_close(out.cpu(), ref["h2"].float() + ws.cpu().float(), what="output")
+    assert_close(ws.cpu()[:H], d32, what="down")
+    assert_close(out.cpu(), ref["h2"].float() + ws.cpu()[:H].float(), what="output")
     assert float((bf16_ulp_diff(out, ref["output"]) > 1).float().mean()) < 0.01
 
 
@@ -104,9 +104,9 @@ def test_layer_post_attn_and_pre_attn(lib):
     o32 = ops.dequant(wo, so) @ attn.float()
     h2 = (hidden.float() + o32.to(BF16).float())
     d32 = ops.dequant(wd, sd) @ bufs[2].cpu().float()
-    assert_close(ws.cpu(), d32, what="down")
+    assert_close(ws.cpu()[:H], d32, what="down")
     assert float((bf16_ulp_diff(out, ref["output"]) > 1).float().mean()) < 0.01
-    assert_close(out.cpu(), h2.to(BF16).float() + ws.cpu().float(), what="output")
+    assert_close(out.cpu(), h2.to(BF16).float() + ws.cpu()[:H].float(), what="output")
 
     # layer_pre_attn: norm_ws = RMSNorm(hidden), then q/k/v GEMVs
     wq, sq = synth.fp8_weight(8192, H, g)
