@@ -150,6 +150,22 @@ int qwen_attn_decode(const void* q_all, const void* k_new, const void* v_new, co
                      float eps, int chunk, int nsplit, float* ws_part, unsigned* ws_count, void* out,
                      cudaStream_t stream);
 
+/* qwen_attn_decode without caller-provided scratch: no counterpart in the
+ * reference.  For callers that cannot allocate device memory where they decode
+ * (a runtime whose pool owns the GPU, a binding without a device allocator,
+ * code that must avoid an allocation's implicit synchronisation).  The split
+ * partials and counters live in a 4 MiB array compiled into the library:
+ * 256-byte-rounded n_heads*nsplit*(head_dim+2)*4 bytes + 4*n_kv_heads bytes
+ * must fit, else cudaErrorInvalidValue and nothing is launched.  The first
+ * call on a device looks the array's address up for that device (make it
+ * before any stream capture); calls share the array, so calls that may run
+ * concurrently on the GPU race; the counters are cleared on `stream` before
+ * each launch.  No cudaMalloc/cudaFree. */
+int qwen_attn_decode_noalloc(const void* q_all, const void* k_new, const void* v_new, const float* q_norm,
+                             const float* k_norm, const float* cos, const float* sin, void* k_cache, void* v_cache,
+                             const int* pos, int max_seq, int n_heads, int n_kv_heads, int head_dim, int rotary_dim,
+                             float eps, int chunk, int nsplit, void* out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

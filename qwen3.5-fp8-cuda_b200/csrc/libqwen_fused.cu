@@ -506,3 +506,62 @@ int qwen_attn_decode(const void* q_all, const void* k_new, const void* v_new, co
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free attention decode.
+//
+// Some callers cannot allocate device memory where they run the decode step:
+// a serving runtime that hands out all GPU memory from its own pool and bans
+// cudaMalloc afterwards, a foreign-language binding (ctypes, cgo, JNI) that
+// has no device allocator of its own, or code that must not trigger the
+// implicit device synchronisation an allocation can cause.  For them,
+// qwen_attn_decode_noalloc takes the split-KV scratch from a fixed array
+// compiled into this library instead of from caller-provided buffers.
+//
+// Limit: partials of n_heads * nsplit * (head_dim + 2) floats, rounded up to
+// 256 bytes, plus n_kv_heads counters must fit QWEN_ATTN_NOALLOC_SCRATCH_BYTES
+// (4 MiB); larger requests return cudaErrorInvalidValue and launch nothing.
+// Every GPU that loads the library holds the 4 MiB until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t QWEN_ATTN_NOALLOC_SCRATCH_BYTES = size_t(4) << 20;
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[QWEN_ATTN_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_attn_noalloc_scratch per device.  In host code the
+// array's name is only a host-side handle, so the address is looked up with
+// cudaGetSymbolAddress by the first call on each device (with that device
+// current) and cached here.
+static void* g_attn_noalloc_addr[64];
+
+extern "C" int qwen_attn_decode_noalloc(const void* q_all, const void* k_new, const void* v_new,
+                                        const float* q_norm, const float* k_norm, const float* cos,
+                                        const float* sin, void* k_cache, void* v_cache, const int* pos, int max_seq,
+                                        int n_heads, int n_kv_heads, int head_dim, int rotary_dim, float eps,
+                                        int chunk, int nsplit, void* out, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record(e);
+  if (dev < 0 || dev >= 64) return record(cudaErrorInvalidDevice);
+  if (!g_attn_noalloc_addr[dev]) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_attn_noalloc_scratch);
+    if (e != cudaSuccess) return record(e);
+    g_attn_noalloc_addr[dev] = addr;
+  }
+  if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || nsplit < 1) return record(cudaErrorInvalidValue);
+  const size_t part_bytes = (size_t)n_heads * (size_t)nsplit * (size_t)(head_dim + 2) * sizeof(float);
+  const size_t count_off = (part_bytes + 255) / 256 * 256;
+  const size_t need = count_off + (size_t)n_kv_heads * sizeof(unsigned);
+  if (need > QWEN_ATTN_NOALLOC_SCRATCH_BYTES) return record(cudaErrorInvalidValue);
+  unsigned char* base = static_cast<unsigned char*>(g_attn_noalloc_addr[dev]);
+  unsigned* counts = reinterpret_cast<unsigned*>(base + count_off);
+  // The array keeps whatever the previous call left; the split counters must
+  // start at zero, so clear them on the stream ahead of the kernel.
+  e = cudaMemsetAsync(counts, 0, (size_t)n_kv_heads * sizeof(unsigned), stream);
+  if (e != cudaSuccess) return record(e);
+  return qwen_attn_decode(q_all, k_new, v_new, q_norm, k_norm, cos, sin, k_cache, v_cache, pos, max_seq, n_heads,
+                          n_kv_heads, head_dim, rotary_dim, eps, chunk, nsplit, reinterpret_cast<float*>(base),
+                          counts, out, stream);
+}

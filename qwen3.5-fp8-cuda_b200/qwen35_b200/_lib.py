@@ -62,6 +62,7 @@ NEW_FUSED = {
     "qwen_linear_resid": (I, [P, P, P, I, I, I, P, P, P]),
     "qwen_mlp_gate_up": (I, [P, P, F, P, P, P, P, I, I, I, P, P]),
     "qwen_attn_decode": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, I, I, P, P, P, P]),
+    "qwen_attn_decode_noalloc": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, I, I, P, P]),
 }
 NEW_FP8 = {
     "qwen_fp8_last_error": (I, []),
