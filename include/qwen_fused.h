@@ -99,6 +99,11 @@ int qwen_last_error(void);
 int qwen_get_device_error(unsigned int* out);
 /* Enable (default) or disable programmatic dependent launch in the engine entry points. */
 void qwen_set_pdl(int enable);
+/* Up to four device regions (null / 0 ignored; 16-byte aligned) that the next
+ * engine launch issued on this host thread pulls into L2 while it runs --
+ * normally the weights of the launch after it.  New; no reference counterpart. */
+void qwen_set_prefetch(const void* p0, unsigned long long n0, const void* p1, unsigned long long n1,
+                       const void* p2, unsigned long long n2, const void* p3, unsigned long long n3);
 int qwen_abi_version(void);
 
 /* ---- new compute entry points --------------------------------------------- */

@@ -42,6 +42,7 @@ struct AttnArgs {
   float* ws_part;      // nsplit > 1: [n_heads][nsplit][D + 2]
   unsigned* ws_count;  // nsplit > 1: [n_kv], zero before first use, left zeroed
   bf16* out;           // [n_heads][D]
+  L2Prefetch pf;       // weights of the next launch (see common.cuh)
 };
 
 constexpr int ATTN_WARPS = 8;
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
   const int kh = blockIdx.x, split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) pdl_trigger();
+  if (warp == 0) l2_prefetch_share(a.pf, lane);
   pdl_wait();
 
   const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_const;

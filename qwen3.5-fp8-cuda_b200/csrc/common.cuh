@@ -55,6 +55,14 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
   return out;
 }
 
+// Two floats -> two E4M3 bytes (round to nearest even, saturating); `lo`
+// goes to the low byte.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  unsigned short out;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(out) : "f"(hi), "f"(lo));
+  return (uint32_t)out;
+}
+
 __device__ __forceinline__ float2 h2u_to_f2(uint32_t h) {
   __half2 v = *reinterpret_cast<__half2*>(&h);
   return __half22float2(v);
@@ -142,6 +150,41 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 }
 
 // ---------------------------------------------------------------------------
+// Look-ahead L2 prefetch.  A decode-step kernel is handed the weight regions of
+// the launch that follows it and pulls its share of them into L2 (bulk
+// prefetch, no shared-memory destination, no completion to wait for) while it
+// runs, so consecutive kernels keep HBM busy across their boundaries.  The
+// regions are static weights, so this is safe before griddepcontrol.wait.
+// ---------------------------------------------------------------------------
+struct L2Prefetch {
+  const void* p[4];
+  unsigned long long n[4];  // bytes, multiples of 16; p 16-byte aligned
+};
+
+// Called by one warp of every CTA: the CTA prefetches a 1/gridDim.x share of
+// each region in pieces of up to 32 KB, one piece per lane at a time.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf, int lane) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const unsigned long long total = pf.n[r];
+    if (total == 0 || pf.p[r] == nullptr) continue;
+    unsigned long long per = (total + gridDim.x - 1) / gridDim.x;
+    per = (per + 15) & ~15ull;
+    const unsigned long long beg = (unsigned long long)blockIdx.x * per;
+    const unsigned long long end = beg + per < total ? beg + per : total;
+    const char* base = static_cast<const char*>(pf.p[r]);
+    for (unsigned long long off = beg + (unsigned long long)lane * 32768ull; off < end; off += 32ull * 32768ull) {
+      const unsigned long long rem = end - off;
+      const uint32_t len = (uint32_t)(rem < 32768ull ? rem : 32768ull);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(base + off), "r"(len) : "memory");
+    }
+  }
+}
+
+// 2^e as a float for |e| <= 126 (exact).
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
+
+// ---------------------------------------------------------------------------
 // Programmatic dependent launch (PDL)
 // ---------------------------------------------------------------------------
 // Block until the grids this grid depends on have completed and flushed.
@@ -156,6 +199,26 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
+// Same, with an L2 eviction-priority policy (evict_first for data read once).
+__device__ __forceinline__ uint4 ld_nc_v4_policy(const void* p, uint64_t policy) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(policy));
+  return r;
+}
+// 16-byte async copy global -> shared (L1 bypass, L2 cache policy).  With
+// ok == false nothing is read and the destination is zero-filled.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool ok, uint64_t policy) {
+  const uint32_t n = ok ? 16u : 0u;
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;"
+               :: "r"(dst), "l"(src), "r"(n), "l"(policy) : "memory");
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "l"(policy) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 __device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
   uint4 r;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"

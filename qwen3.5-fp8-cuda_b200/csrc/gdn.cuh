@@ -35,6 +35,7 @@ struct GdnArgs {
   float eps;
   int rep;             // value heads per key head
   int gated;
+  L2Prefetch pf;       // weights of the next launch (see common.cuh)
 };
 
 template <int D, int KG>
@@ -50,8 +51,9 @@ __global__ void __launch_bounds__(D * KG) gdn_decode_kernel(const __grid_constan
   const int lane = tid & 31, warp = tid >> 5;
 
   if (tid == 0) pdl_trigger();
-  // Independent of earlier kernels? No: q/k/v/g/beta come from the projection
-  // kernel and the state from the previous step, so wait before any load.
+  if (tid < 32) l2_prefetch_share(a.pf, tid);
+  // q/k/v/g/beta come from the projection kernel and the state from the
+  // previous step, so every load below waits for the previous grid.
   pdl_wait();
 
   float* S = a.state + (size_t)h * D * D;

@@ -7,21 +7,31 @@
 // Restates gemv_v4_kernel and its fused variants (fused_kernels.cu:91-479) as
 // an HBM stream:
 //
-//  * rows are contiguous, so a tile of `rs` rows x K bytes is one contiguous
-//    range; a producer warp moves tiles into a shared-memory ring with 1-D
-//    bulk async copies (cp.async.bulk, no multicast) completing on mbarriers;
-//  * consumer warps keep their slice of x in registers for the whole kernel
-//    (loaded once) and read the weights from shared memory, 16 bytes a lane;
-//  * the scale is applied once per 16-element chunk into FP32 accumulators;
-//  * one CTA per SM, persistent over tiles; with programmatic dependent
-//    launch the producer prefetches the first tiles before waiting on the
-//    previous kernel, so weight streaming continues across kernel boundaries.
+//  * a warp owns a tile of 8 weight rows (8 gate + 8 up rows for the paired
+//    MLP) and a range of 128-wide K blocks; each lane streams 16 contiguous
+//    bytes of one row per 64-K step with ld.global.nc (L1 bypass, L2
+//    evict-first), a batch of JB steps in flight before any is consumed;
+//  * the inner products run on the tensor cores as FP8 MMAs
+//    (mma.sync m16n8k32 e4m3 x e4m3 -> f32): the weights are the B operand
+//    exactly as stored; x is the A operand, split in two E4M3 terms, hi in
+//    A rows 0-7 and lo in rows 8-15, so one MMA yields both partial sums; a
+//    fixed permutation of K inside each 32-K step makes one 16-byte load per
+//    lane exactly the lane's B fragments of two MMAs, and one 16-byte shared
+//    load exactly its A fragment of one;
+//  * x is staged once per CTA in shared memory as E4M3 pairs per 128-K
+//    block, x * 2^e = hi + lo / 32, with e chosen so that the block's largest
+//    magnitude lands in [2^7, 2^8): hi + lo / 32 equals the BF16 value
+//    exactly for every element within 2^-14 of that maximum and to within
+//    2^-15 absolute (2^-22 of the maximum) below it.  The hi and lo rows of
+//    the MMA result are combined in FP32 and the block scale times 2^-e is
+//    applied once per 128-K block;
+//  * when a launch has fewer tiles than resident warps, the warps of a CTA
+//    split K and add their partial sums through shared memory;
+//  * the first batch of weight loads and a look-ahead L2 prefetch of the next
+//    launch's weights are issued before griddepcontrol.wait.
 //
-// Dot-product arithmetic: E4M3 pairs are widened exactly to f16x2 with
-// cvt.rn.f16x2.e4m3x2.  x is held as f16 scaled by a power of two per
-// 128-wide K block (exact for every element within 2^-32 of the block's
-// largest magnitude), products are formed by the mixed-precision
-// fma.rn.f32.f16, and the power of two is folded into the block scale.
+// Products are exact (E4M3 x E4M3) and sums are FP32, as in the reference;
+// the summation order and the split of x are the only differences.
 #pragma once
 
 #include "common.cuh"
@@ -29,6 +39,16 @@
 namespace qwen {
 
 constexpr int GEMV_MAX_SEG = 6;
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+#ifndef GEMV_CTAS_PER_SM
+#define GEMV_CTAS_PER_SM 3     // resident CTAs per SM
+#endif
+#ifndef GEMV_RING_BYTES
+#define GEMV_RING_BYTES 8192   // per-warp cp.async ring (2 stages of 4 KB)
+#endif
+constexpr int GEMV_NORM_REG_BLOCKS = 3;  // RMSNorm weights held in registers for K <= 3072
+constexpr int GEMV_TILE = 8;  // weight rows per warp work unit (the N of one MMA)
 
 enum GemvEpi : int {
   EPI_STORE = 0,      // y[r] = bf16(v)
@@ -60,7 +80,7 @@ struct GemvSeg {
   int n;
   int kblk;
   int epi;
-  int tile0;          // first tile index of this segment (filled by the planner)
+  int unit0;          // first work unit of this segment (filled by the planner)
   int row_offset;     // ARGMAX: global index of row 0 (vocabulary shard offset)
   int cw;             // CONV: kernel width (<= 8)
 };
@@ -76,30 +96,35 @@ struct GemvArgs {
   int K;
   int pro;
   int nseg;
-  int ntiles;
-  int rs, npart, nslice, nstages, stage_bytes;
+  int nunits;          // total work units (filled by the planner)
+  int nslice;          // warps sharing one tile (K split), divides GEMV_WARPS
   unsigned long long* am_ws;       // ARGMAX workspace {key, count}: zero before first use, left zeroed
   unsigned long long* am_key_out;  // optional: final packed key
   long long* am_token_out;         // optional: final token id
   int* pos_inc;                    // optional: ++*pos_inc by the argmax finaliser
+  L2Prefetch pf;                   // weights of the next launch, pulled into L2 while this one runs
   GemvSeg seg[GEMV_MAX_SEG];
 };
 
-// ---------------------------------------------------------------------------
-// Shared-memory layout of the streaming kernel (host and device agree).
-// ---------------------------------------------------------------------------
-struct GemvSmem {
-  int x_off, ex_off, red_off, misc_off, bar_off, total;
-};
 __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
-__host__ __device__ inline GemvSmem gemv_smem_layout(int K, int nstages, int stage_bytes, int rs, int npart) {
+
+// Shared memory of the MMA kernel: x (BF16 staging, then in place the E4M3
+// hi / lo words, 256 bytes per 128-K block: elements 4l..4l+3 of the block
+// as {hi word, lo word} at byte 8l, which is where they were staged), the
+// per-128-block 2^-e factors, slice partials, a small reduction area and one
+// cp.async ring per warp.
+struct GemvSmem {
+  int x8_off, xinv_off, red_off, misc_off, ring_off, total;
+};
+__host__ __device__ inline GemvSmem gemv_smem_layout(int K) {
   GemvSmem L;
-  L.x_off = nstages * stage_bytes;                       // stages first: 128-byte aligned base
-  L.ex_off = align_up(L.x_off + 2 * K, 16);              // per-128-block x exponents (int32)
-  L.red_off = align_up(L.ex_off + 4 * ((K + 127) / 128), 16);
-  L.misc_off = align_up(L.red_off + 4 * nstages * rs * npart, 16);
-  L.bar_off = align_up(L.misc_off + 8 * 64, 16);
-  L.total = L.bar_off + 16 * nstages;
+  const int nb = (K + 127) / 128;
+  L.x8_off = 0;
+  L.xinv_off = align_up(2 * K, 16);
+  L.red_off = align_up(L.xinv_off + 4 * nb, 16);
+  L.misc_off = L.red_off + 4 * 2 * GEMV_WARPS * GEMV_TILE * 2;
+  L.ring_off = L.misc_off + 8 * 64;
+  L.total = L.ring_off + GEMV_WARPS * GEMV_RING_BYTES;
   return L;
 }
 
@@ -126,8 +151,9 @@ __device__ __forceinline__ float load_scale(const void* s, int idx) {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-__device__ __noinline__ void gemv_epilogue(const GemvSeg& sg, int r, float v, float v2,
-                                           unsigned long long& am_best) {
+// Returns the updated running argmax key (EPI_ARGMAX).
+__device__ __noinline__ unsigned long long gemv_epilogue(const GemvSeg& sg, int r, float v, float v2,
+                                                         unsigned long long am_best) {
   switch (sg.epi) {
     case EPI_STORE:
       reinterpret_cast<bf16*>(sg.y)[r] = f2bf(v);
@@ -135,7 +161,7 @@ __device__ __noinline__ void gemv_epilogue(const GemvSeg& sg, int r, float v, fl
     case EPI_RESID: {
       bf16 d = f2bf(v);
       if (sg.y2) reinterpret_cast<bf16*>(sg.y2)[r] = d;
-      float res = bf2f(reinterpret_cast<const bf16*>(sg.aux0)[r]);
+      const float res = bf2f(reinterpret_cast<const bf16*>(sg.aux0)[r]);
       reinterpret_cast<bf16*>(sg.y)[r] = f2bf(res + bf2f(d));
     } break;
     case EPI_SILU_PAIR:
@@ -180,6 +206,7 @@ __device__ __noinline__ void gemv_epilogue(const GemvSeg& sg, int r, float v, fl
     default:
       break;
   }
+  return am_best;
 }
 
 __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int o) {
@@ -264,223 +291,404 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, bf16* xs, float
   named_bar(bar, nthr);
 }
 
-// Power-of-two exponent per 128-wide block of x so that max|x| * 2^e lies in
-// [2^14, 2^15): x * 2^e is then exact in f16 for every element >= max * 2^-32.
-__device__ __forceinline__ void gemv_x_exponents(const bf16* xs, int* ex, int K, int tid, int nthr, int bar) {
-  const int nb = (K + 127) / 128;
-  const int lane = tid & 31, w = tid >> 5, nw = nthr >> 5;
-  for (int b = w; b < nb; b += nw) {
-    float m = 0.f;
-    for (int i = b * 128 + lane; i < min(K, b * 128 + 128); i += 32) m = fmaxf(m, fabsf(bf2f(xs[i])));
-    m = warp_max(m);
-    if (lane == 0) {
-      int e = 0;
-      if (m > 0.f) {
-        int E;
-        frexpf(m, &E);  // m = f * 2^E, f in [0.5, 1)
-        e = 15 - E;
-        e = e < -100 ? -100 : (e > 100 ? 100 : e);
-      }
-      ex[b] = e;
-    }
-  }
-  named_bar(bar, nthr);
-}
-
-// Mixed-precision multiply-add of 16 E4M3 weights with 16 f16 x values.
-__device__ __forceinline__ void dot16_f16(const uint4 w, const uint32_t (&xh)[8], float& a0, float& a1) {
-  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+// RMSNorm weights of the first GEMV_NORM_REG_BLOCKS 128-blocks a warp
+// normalises (static data: loaded before griddepcontrol.wait).
+struct NormRegs {
+  float4 w[GEMV_NORM_REG_BLOCKS];
+};
+__device__ __forceinline__ void gemv_norm_preload(const GemvArgs& a, NormRegs& nr) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nb = a.K >> 7;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t h01 = e4m3x2_to_f16x2(ww[i]);
-    const uint32_t h23 = e4m3x2_to_f16x2(ww[i] >> 16);
-    asm("{\n .reg .b16 w0, w1, x0, x1;\n"
-        " mov.b32 {w0, w1}, %2;\n mov.b32 {x0, x1}, %3;\n"
-        " fma.rn.f32.f16 %0, w0, x0, %0;\n fma.rn.f32.f16 %1, w1, x1, %1;\n}\n"
-        : "+f"(a0), "+f"(a1) : "r"(h01), "r"(xh[2 * i]));
-    asm("{\n .reg .b16 w0, w1, x0, x1;\n"
-        " mov.b32 {w0, w1}, %2;\n mov.b32 {x0, x1}, %3;\n"
-        " fma.rn.f32.f16 %0, w0, x0, %0;\n fma.rn.f32.f16 %1, w1, x1, %1;\n}\n"
-        : "+f"(a0), "+f"(a1) : "r"(h23), "r"(xh[2 * i + 1]));
+  for (int i = 0; i < GEMV_NORM_REG_BLOCKS; ++i) {
+    const int b = warp + i * GEMV_WARPS;
+    nr.w[i] = (a.pro != PRO_NONE && b < nb) ? __ldg(reinterpret_cast<const float4*>(a.norm_w + b * 128) + lane)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
-__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
+// Kernel prologue (K % 128 == 0), two passes and two barriers:
+//  1. all threads, 8 elements each: x (+ x2) -> BF16 into the x8 area, sum
+//     of squares for RMSNorm;
+//  2. one warp per 128-wide block, 4 elements per lane, in place: RMSNorm(1+w)
+//     (BF16 rounded), exponent e with max|x| * 2^e in [2^7, 2^8), x * 2^e
+//     split into E4M3 hi + lo / 32 (hi = RN(x * 2^e), lo = RN(32 (x * 2^e -
+//     hi))) and 2^-e per block (xinv).  Each lane overwrites exactly the 8 bytes it
+//     staged: {hi word, lo word} of its 4 elements.
+__device__ __forceinline__ void gemv_x_prepare(const GemvArgs& a, const NormRegs& nr, uint8_t* x8raw, float* xinv,
+                                               float* red32) {
+  const int K = a.K;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bf16* xin = a.x;
+  if (a.x_row) xin += (size_t)(*a.x_row) * K;
+  uint4* xs8 = reinterpret_cast<uint4*>(x8raw);
+  float ss = 0.f;
+  for (int i = tid; i < (K >> 3); i += GEMV_THREADS) {
+    uint4 v = __ldg(reinterpret_cast<const uint4*>(xin) + i);
+    if (a.pro == PRO_ADD_RMSNORM) {
+      const uint4 r = __ldg(reinterpret_cast<const uint4*>(a.x2) + i);
+      uint32_t* vw = reinterpret_cast<uint32_t*>(&v);
+      const uint32_t* rw = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = bf2x_to_f2(vw[t]), g = bf2x_to_f2(rw[t]);
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f.x + g.x, f.y + g.y);
+        vw[t] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      if (blockIdx.x == 0 && a.h2_out) reinterpret_cast<uint4*>(a.h2_out)[i] = v;
+    }
+    const uint32_t* vw = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 f = bf2x_to_f2(vw[t]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+    xs8[i] = v;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red32[warp] = ss;
+  __syncthreads();
+  float rms = 1.f;
+  if (a.pro != PRO_NONE) {
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < GEMV_WARPS; ++i) tot += red32[i];
+    rms = rsqrtf(tot / (float)K + a.eps);
+  }
+  const int nb = K >> 7;
+  for (int b = warp, i = 0; b < nb; b += GEMV_WARPS, ++i) {
+    const uint2 raw = reinterpret_cast<const uint2*>(x8raw)[b * 32 + lane];
+    const float2 v01 = bf2x_to_f2(raw.x), v23 = bf2x_to_f2(raw.y);
+    float v[4] = {v01.x, v01.y, v23.x, v23.y};
+    if (a.pro != PRO_NONE) {
+      float4 w;
+      if (i < GEMV_NORM_REG_BLOCKS) {
+        w = nr.w[0];
+#pragma unroll
+        for (int j = 1; j < GEMV_NORM_REG_BLOCKS; ++j)
+          if (i == j) w = nr.w[j];
+      } else {
+        w = __ldg(reinterpret_cast<const float4*>(a.norm_w + b * 128) + lane);
+      }
+      const float wv[4] = {w.x, w.y, w.z, w.w};
+      bf16 o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        o[t] = f2bf(v[t] * rms * (1.0f + wv[t]));
+        v[t] = bf2f(o[t]);
+      }
+      if (blockIdx.x == 0 && a.xn_out) {
+        uint2 ov;
+        ov.x = (uint32_t)__bfloat16_as_ushort(o[0]) | ((uint32_t)__bfloat16_as_ushort(o[1]) << 16);
+        ov.y = (uint32_t)__bfloat16_as_ushort(o[2]) | ((uint32_t)__bfloat16_as_ushort(o[3]) << 16);
+        reinterpret_cast<uint2*>(a.xn_out)[b * 32 + lane] = ov;
+      }
+    }
+    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    m = warp_max(m);
+    // m = 1.f * 2^(ebits - 127): e = 134 - ebits puts m * 2^e in [2^7, 2^8)
+    // (denormal m: e = 100, far below anything that matters)
+    const int ebits = (int)((__float_as_uint(m) >> 23) & 0xffu);
+    int e = m > 0.f ? (ebits == 0 ? 100 : 134 - ebits) : 0;
+    e = e < -100 ? -100 : (e > 100 ? 100 : e);
+    const float sc = exp2i(e);
+    float xs[4], hi[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) xs[t] = v[t] * sc;
+    const uint32_t h01 = f32x2_to_e4m3x2(xs[0], xs[1]), h23 = f32x2_to_e4m3x2(xs[2], xs[3]);
+    const float2 g01 = h2u_to_f2(e4m3x2_to_f16x2(h01)), g23 = h2u_to_f2(e4m3x2_to_f16x2(h23));
+    hi[0] = g01.x; hi[1] = g01.y; hi[2] = g23.x; hi[3] = g23.y;
+    // lo carries 32 * (x * 2^e - hi): |x * 2^e - hi| <= 8, so 32x stays below 448
+    const uint32_t l01 = f32x2_to_e4m3x2((xs[0] - hi[0]) * 32.f, (xs[1] - hi[1]) * 32.f);
+    const uint32_t l23 = f32x2_to_e4m3x2((xs[2] - hi[2]) * 32.f, (xs[3] - hi[3]) * 32.f);
+    reinterpret_cast<uint2*>(x8raw)[b * 32 + lane] = make_uint2(h01 | (h23 << 16), l01 | (l23 << 16));
+    if (lane == 0) xinv[b] = exp2i(-e);
+  }
+  __syncthreads();
 }
 
-__device__ __forceinline__ int gemv_find_seg(const GemvArgs& a, int t) {
+// D (16x8, f32) (+)= A (16x32 E4M3, row) * B (32x8 E4M3, col): one FP8
+// tensor-core MMA; a = {a0, a1, a2, a3} is the lane's A fragment as loaded.
+// The _zc form starts from a zero accumulator.
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_e4m3_zc(float (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%10,%10,%10,%10};"
+               : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+               : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+__device__ __forceinline__ int gemv_find_seg(const GemvArgs& a, int u) {
   int s = 0;
 #pragma unroll
   for (int i = 1; i < GEMV_MAX_SEG; ++i)
-    if (i < a.nseg && t >= a.seg[i].tile0) s = i;
+    if (i < a.nseg && u >= a.seg[i].unit0) s = i;
   return s;
 }
 
+// One work unit: two 8-row tiles, p = 0, 1.  For a gate/up pair they are
+// the same 8 rows of the gate and the up matrix; otherwise 16 consecutive
+// rows of one matrix.  w[p] points at tile p's first row.
+struct GemvTile {
+  const uint8_t* w[2];
+  int r0[2];     // output row of tile p's first row
+  int nrows[2];  // valid rows in tile p (0..8)
+  int seg;
+};
+
+template <bool PAIR>
+__device__ __forceinline__ GemvTile gemv_tile(const GemvArgs& a, int u) {
+  GemvTile T;
+  T.seg = gemv_find_seg(a, u);
+  const GemvSeg& sg = a.seg[T.seg];
+  const int K = a.K;
+  if (PAIR) {
+    const int row0 = (u - sg.unit0) * GEMV_TILE;
+    T.r0[0] = T.r0[1] = row0;
+    T.nrows[0] = T.nrows[1] = min(GEMV_TILE, sg.n - row0);
+    T.w[0] = sg.w + (size_t)row0 * K;
+    T.w[1] = sg.w2 + (size_t)row0 * K;
+  } else {
+    const int row0 = (u - sg.unit0) * 2 * GEMV_TILE;
+    T.r0[0] = row0;
+    T.r0[1] = row0 + GEMV_TILE;
+    T.nrows[0] = min(GEMV_TILE, sg.n - row0);
+    T.nrows[1] = max(0, min(GEMV_TILE, sg.n - row0 - GEMV_TILE));
+    T.w[0] = sg.w + (size_t)row0 * K;
+    T.w[1] = T.nrows[1] > 0 ? T.w[0] + (size_t)GEMV_TILE * K : T.w[0];
+  }
+  return T;
+}
+
+// Block-mode scales of one unit for the 128-K blocks of a slice: lane l
+// holds scale[row0 / 128, kb0 + l] of tile p (l < nkbs <= 32).  Both tiles of
+// an unpaired unit lie in one 128-row block.
+template <typename ST, bool PAIR>
+__device__ __forceinline__ void gemv_unit_scales(const GemvArgs& a, int u, int kb0, int nkbs, float (&sc)[2]) {
+  const int lane = threadIdx.x & 31;
+  sc[0] = sc[1] = 0.f;
+  if (u >= a.nunits || lane >= nkbs) return;
+  const GemvSeg& sg = a.seg[gemv_find_seg(a, u)];
+  const int row0 = (u - sg.unit0) * (PAIR ? GEMV_TILE : 2 * GEMV_TILE);
+  const int idx = (row0 >> 7) * sg.kblk + kb0 + lane;
+  sc[0] = load_scale<ST>(sg.s, idx);
+  sc[1] = PAIR ? load_scale<ST>(sg.s2, idx) : sc[0];
+}
+
 // ---------------------------------------------------------------------------
-// Streaming kernel: NC consumer warps + 1 producer warp, J 16-byte chunks of
-// each row per lane (K = 512 * J * nslice).
+// Tensor-core streaming GEMV over units of two 8-row tiles (block-mode
+// scales only; the planner sends the other scale layouts to the generic
+// kernel).  The CTA's warps form groups of S = a.nslice warps; a group works
+// on one unit at a time and its warps split the unit's 128-K blocks (at most
+// 32 per warp), reducing through shared memory.  Each warp is its own
+// producer and consumer: a stage is two 128-K blocks of the unit's 16 rows
+// (4 KB), copied with cp.async so that every instruction reads 256
+// contiguous bytes of each of two rows, and placed in shared memory where
+// each lane finds its MMA fragments with one 16-byte load; the warp keeps
+// R - 1 stages of loads in flight ahead of the stage it multiplies.
 // ---------------------------------------------------------------------------
-template <typename ST, int NC, int J>
-__global__ void __launch_bounds__((NC + 1) * 32, 2) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
+template <typename ST, bool PAIR>
+__global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) gemv_mma_kernel(const __grid_constant__ GemvArgs a) {
+  constexpr int STAGE = 4096;  // 2 K-blocks x 2 tiles x 8 rows x 128 B
+  constexpr int R = GEMV_RING_BYTES / STAGE;
+  static_assert(R >= 2, "ring too small");
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K;
+  const int nkb = K >> 7;  // K % 128 == 0 on this path
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ns = a.nstages, sb = a.stage_bytes, rs = a.rs, npart = a.npart, nslice = a.nslice;
-  const GemvSmem L = gemv_smem_layout(K, ns, sb, rs, npart);
-  bf16* xs = reinterpret_cast<bf16*>(smem + L.x_off);
-  int* ex = reinterpret_cast<int*>(smem + L.ex_off);
-  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  const int gq = lane >> 2, tq = lane & 3;  // MMA groupID / thread-in-group
+  const GemvSmem L = gemv_smem_layout(K);
+  const uint32_t x8 = smem_u32(smem + L.x8_off) + tq * 32;
+  const float* xinv = reinterpret_cast<const float*>(smem + L.xinv_off);
+  float* red = reinterpret_cast<float*>(smem + L.red_off);  // [2][GEMV_WARPS][GEMV_TILE][2]
   unsigned long long* misc = reinterpret_cast<unsigned long long*>(smem + L.misc_off);
-  const uint32_t bar0 = smem_u32(smem + L.bar_off);  // full[s] at bar0+8s, empty[s] at bar0+8(ns+s)
-  const uint32_t stage0 = smem_u32(smem);
+  const uint32_t ring = smem_u32(smem + L.ring_off) + warp * GEMV_RING_BYTES;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < ns; ++s) {
-      mbar_init(bar0 + 8 * s, 1);
-      mbar_init(bar0 + 8 * (ns + s), NC);
+  const int S = a.nslice;
+  const int G = GEMV_WARPS / S;
+  const int g = warp / S, sl = warp % S;
+  const int kb0 = (sl * nkb) / S, kb1 = ((sl + 1) * nkb) / S;
+  const int nkbs = kb1 - kb0;          // 128-K blocks of this slice (1..32)
+  const int nst = (nkbs + 1) >> 1;     // stages of this slice
+  const int ngroups = gridDim.x * G;
+  const uint64_t pol = l2_policy_evict_first();  // weights are read once per step
+
+  // Producer.  Copy instruction i (0..7) of a stage covers unit rows 2i and
+  // 2i+1, i.e. tile p = i / 4, rows 2 (i % 4) + lane / 16; lane moves bytes
+  // 16 (lane % 16) .. +15 of the stage's 256-byte row piece, which are
+  // K-block bi, half h, MMA column group tq' of that row.  Its shared-memory
+  // slot is the one lane (row, tq') reads for (bi, tile, h).
+  const int prow = lane >> 4, pbi = (lane >> 3) & 1;
+  const uint32_t pdst = ring + pbi * 2048 + ((lane >> 2) & 1) * 512 + (prow * 4 + (lane & 3)) * 16;
+  const size_t K2 = (size_t)2 * K;
+  int up = blockIdx.x * G + g, qp = 0, ps = 0;
+  const uint8_t* pw[2];
+  int pn[2];
+  auto producer_unit = [&]() {
+    const GemvTile T = gemv_tile<PAIR>(a, up);
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      pn[p] = T.nrows[p];
+      pw[p] = T.w[p] + (size_t)prow * K + (size_t)kb0 * 128 + (lane & 15) * 16;
     }
-    mbar_fence_init();
-  }
-  __syncthreads();
+  };
+  if (up < a.nunits) producer_unit();
+  auto produce = [&]() {
+    if (up < a.nunits) {
+      const uint32_t dst = pdst + ps * STAGE;
+      if (pn[0] == GEMV_TILE && pn[1] == GEMV_TILE && 2 * qp + 1 < nkbs) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const uint8_t* src = pw[p];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) cp_async16(dst + p * 1024 + i * 128, src + i * K2, pol);
+        }
+      } else {
+        // ragged unit (rows past the segment end) or a single-block stage
+        const bool kok = 2 * qp + pbi < nkbs;
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const bool ok = kok && 2 * i + prow < pn[p];
+            cp_async16(dst + p * 1024 + i * 128, ok ? pw[p] + i * K2 : pw[0], ok, pol);
+          }
+      }
+      pw[0] += 256;
+      pw[1] += 256;
+      if (++qp == nst) {
+        qp = 0;
+        up += ngroups;
+        if (up < a.nunits) producer_unit();
+      }
+    }
+    cp_async_commit();
+    ps = ps + 1 == R ? 0 : ps + 1;
+  };
+
+  // Weights and scales are static: start streaming before waiting on the
+  // previous kernel.
   if (threadIdx.x == 0) pdl_trigger();
+#pragma unroll 1
+  for (int i = 0; i < R - 1; ++i) produce();
+  int uc = blockIdx.x * G + g, qc = 0, cs = 0;
+  float sc[2], sc_next[2];
+  gemv_unit_scales<ST, PAIR>(a, uc, kb0, nkbs, sc);
+  gemv_unit_scales<ST, PAIR>(a, uc + ngroups, kb0, nkbs, sc_next);
+  NormRegs nr;
+  gemv_norm_preload(a, nr);
+  if (warp == 0) l2_prefetch_share(a.pf, lane);
+  pdl_wait();
+  gemv_x_prepare(a, nr, smem + L.x8_off, const_cast<float*>(xinv), reinterpret_cast<float*>(misc));
 
   unsigned long long am_best = 0ull;
+  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  int parity = 0;
 
-  if (warp == NC) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_first();
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++it) {
-        const int slot = it % ns;
-        if (it >= ns) {
-          if (!mbar_wait_bounded(bar0 + 8 * (ns + slot), ((it / ns) & 1) ^ 1)) {
-            qwen_err_set(ERR_TIMEOUT_EMPTY);
-            ok = false;
-            break;
+  // One 128-K block of both tiles: 8 MMAs, then promotion with the block
+  // scale and 2^-e of x.  Rows 0-7 of D carry the hi products, rows 8-15 the
+  // lo products (x 32).
+  auto consume_block = [&](uint32_t src, int kbl) {
+    const int kb = kb0 + kbl;
+    float d[2][2][4];  // [tile][MMA j of a 32-K pair][fragment]
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      // A fragments of this lane for K offset kb*128 + 64h + 16tq + 8j:
+      // {hi, lo, hi, lo} words, one 16-byte load per j
+      const uint4 xa0 = lds_v4(x8 + kb * 256 + h * 128);
+      const uint4 xa1 = lds_v4(x8 + kb * 256 + h * 128 + 16);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const uint4 wv = lds_v4(src + p * 1024 + h * 512);
+        if (h == 0) {
+          mma_e4m3_zc(d[p][0], xa0, wv.x, wv.y);
+          mma_e4m3_zc(d[p][1], xa1, wv.z, wv.w);
+        } else {
+          mma_e4m3(d[p][0], xa0, wv.x, wv.y);
+          mma_e4m3(d[p][1], xa1, wv.z, wv.w);
+        }
+      }
+    }
+    const float f = xinv[kb];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const float sf = __shfl_sync(0xffffffffu, sc[p], kbl) * f;
+      const float v0 = (d[p][0][0] + d[p][1][0]) + (d[p][0][2] + d[p][1][2]) * 0.03125f;
+      const float v1 = (d[p][0][1] + d[p][1][1]) + (d[p][0][3] + d[p][1][3]) * 0.03125f;
+      acc[p][0] = fmaf(v0, sf, acc[p][0]);
+      acc[p][1] = fmaf(v1, sf, acc[p][1]);
+    }
+  };
+
+#pragma unroll 1
+  while (uc < a.nunits) {
+    __syncwarp();  // every lane is done reading the slot that produce() refills
+    produce();
+    cp_async_wait<R - 1>();
+    __syncwarp();  // the stage was copied by other lanes of this warp
+    const uint32_t src = ring + cs * STAGE + lane * 16;
+    cs = cs + 1 == R ? 0 : cs + 1;
+    consume_block(src, 2 * qc);
+    if (2 * qc + 1 < nkbs) consume_block(src + 2048, 2 * qc + 1);
+    if (++qc == nst) {
+      // unit finished: lanes 0..3 hold rows 2*tq, 2*tq+1 of both tiles
+      const GemvTile T = gemv_tile<PAIR>(a, uc);
+      const GemvSeg& sg = a.seg[T.seg];
+      bool lead = true;
+      if (S > 1) {
+        float* rb = red + (parity * GEMV_WARPS + warp) * GEMV_TILE * 2;
+        if (gq == 0) {
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            rb[(2 * tq) * 2 + p] = acc[p][0];
+            rb[(2 * tq + 1) * 2 + p] = acc[p][1];
           }
         }
-        const int si = gemv_find_seg(a, t);
-        const GemvSeg& sg = a.seg[si];
-        const int row0 = (t - sg.tile0) * rs;
-        const int nrows = min(rs, sg.n - row0);
-        const uint32_t bytes = (uint32_t)nrows * (uint32_t)K;
-        const bool paired = sg.epi == EPI_SILU_PAIR;
-        mbar_arrive_expect_tx(bar0 + 8 * slot, paired ? 2 * bytes : bytes);
-        const uint32_t dst = stage0 + slot * sb;
-        bulk_g2s(dst, sg.w + (size_t)row0 * K, bytes, bar0 + 8 * slot, pol);
-        if (paired) bulk_g2s(dst + rs * K, sg.w2 + (size_t)row0 * K, bytes, bar0 + 8 * slot, pol);
-      }
-      // Drain: every issued copy must have landed before this thread leaves.
-      const int issued = it;
-      for (int j = issued - ns; j < issued; ++j) {
-        if (j < 0) continue;
-        if (!mbar_wait_bounded(bar0 + 8 * (j % ns), (j / ns) & 1)) {
-          qwen_err_set(ERR_TIMEOUT_DRAIN);
-          break;
-        }
-      }
-      (void)ok;
-    }
-  } else {
-    // ---------------- consumers ----------------
-    const int ctid = threadIdx.x;  // 0 .. NC*32-1
-    const int nthr = NC * 32;
-    pdl_wait();
-    gemv_prologue(a, xs, reinterpret_cast<float*>(misc), ctid, nthr, 1);
-    gemv_x_exponents(xs, ex, K, ctid, nthr, 1);
-
-    const int part = warp % npart;
-    const int mat = part / nslice;
-    const int slice = part % nslice;
-    const int row_step = NC / npart;
-
-    // x slice in registers as f16 (scaled per 128-block), chunk c_j = (slice*J + j)*32 + lane.
-    uint32_t xh[J][8];
+        named_bar(2 + g, S * 32);
+        lead = sl == 0;
+        if (lead && gq == 0) {
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int c = (slice * J + j) * 32 + lane;
-      const int e = ex[c >> 3];
-      const uint4 raw = *reinterpret_cast<const uint4*>(xs + c * 16);
-      const uint4 raw2 = *reinterpret_cast<const uint4*>(xs + c * 16 + 8);
-      const uint32_t u[8] = {raw.x, raw.y, raw.z, raw.w, raw2.x, raw2.y, raw2.z, raw2.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float2 f = bf2x_to_f2(u[i]);
-        xh[j][i] = pack_f16x2(ldexpf(f.x, e), ldexpf(f.y, e));
-      }
-    }
-
-    // After a timed-out wait the warp stops computing but keeps taking part in
-    // every barrier, so a fault degrades to an error code, never a hang.
-    bool failed = false;
-    int it = 0;
-    for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++it) {
-      const int slot = it % ns;
-      if (!failed && !mbar_wait_bounded(bar0 + 8 * slot, (it / ns) & 1)) {
-        qwen_err_set(ERR_TIMEOUT_FULL);
-        failed = true;
-      }
-      const int si = gemv_find_seg(a, t);
-      const GemvSeg& sg = a.seg[si];
-      const int row0 = (t - sg.tile0) * rs;
-      const int nrows = min(rs, sg.n - row0);
-      const void* sp = mat ? sg.s2 : sg.s;
-      const int kblk = sg.kblk;
-      float sc[J];
-      if (kblk > 1) {
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-          const int c = (slice * J + j) * 32 + lane;
-          sc[j] = ldexpf(load_scale<ST>(sp, scale_index(kblk, row0, c >> 3)), -ex[c >> 3]);
-        }
-      }
-      const uint32_t sbase = stage0 + slot * sb + (uint32_t)(mat * rs) * K;
-      for (int ri = warp / npart; ri < rs; ri += row_step) {
-        if (ri < nrows && !failed) {
-          if (kblk <= 1) {
-#pragma unroll
-            for (int j = 0; j < J; ++j) {
-              const int c = (slice * J + j) * 32 + lane;
-              sc[j] = ldexpf(load_scale<ST>(sp, scale_index(kblk, row0 + ri, c >> 3)), -ex[c >> 3]);
+          for (int p = 0; p < 2; ++p) {
+            float t0 = 0.f, t1 = 0.f;
+            for (int q2 = 0; q2 < S; ++q2) {
+              const float* ob = red + (parity * GEMV_WARPS + g * S + q2) * GEMV_TILE * 2;
+              t0 += ob[(2 * tq) * 2 + p];
+              t1 += ob[(2 * tq + 1) * 2 + p];
             }
+            acc[p][0] = t0;
+            acc[p][1] = t1;
           }
-          const uint32_t rbase = sbase + (uint32_t)ri * K;
-          float acc = 0.f;
+        }
+        parity ^= 1;
+      }
+      if (lead && gq == 0) {
 #pragma unroll
-          for (int j = 0; j < J; ++j) {
-            const int c = (slice * J + j) * 32 + lane;
-            const uint4 w = lds_v4(rbase + c * 16);
-            float p0 = 0.f, p1 = 0.f;
-            dot16_f16(w, xh[j], p0, p1);
-            acc = fmaf(p0 + p1, sc[j], acc);
-          }
-          acc = warp_sum(acc);
-          if (npart == 1) {
-            if (lane == 0) gemv_epilogue(sg, row0 + ri, acc, 0.f, am_best);
-          } else if (lane == 0) {
-            red[(slot * rs + ri) * npart + part] = acc;
+        for (int i = 0; i < 2; ++i) {
+          const int r = 2 * tq + i;
+          if (PAIR) {
+            if (r < T.nrows[0]) am_best = gemv_epilogue(sg, T.r0[0] + r, acc[0][i], acc[1][i], am_best);
+          } else {
+#pragma unroll
+            for (int p = 0; p < 2; ++p)
+              if (r < T.nrows[p]) am_best = gemv_epilogue(sg, T.r0[p] + r, acc[p][i], 0.f, am_best);
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar0 + 8 * (ns + slot));
-      if (npart > 1) {
-        named_bar(1, nthr);
-        if (ctid < nrows && !failed) {
-          const float* rr = red + (slot * rs + ctid) * npart;
-          float v = 0.f, v2 = 0.f;
-          for (int s = 0; s < nslice; ++s) v += rr[s];
-          if (npart > nslice)
-            for (int s = 0; s < nslice; ++s) v2 += rr[nslice + s];
-          gemv_epilogue(sg, row0 + ctid, v, v2, am_best);
-        }
-      }
+      acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+      qc = 0;
+      uc += ngroups;
+      sc[0] = sc_next[0];
+      sc[1] = sc_next[1];
+      gemv_unit_scales<ST, PAIR>(a, uc + ngroups, kb0, nkbs, sc_next);
     }
   }
+  cp_async_wait<0>();
 
   if (a.am_ws) argmax_finish(a, am_best, misc + 32);
 }
@@ -488,7 +696,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2) gemv_stream_kernel(const __g
 // ---------------------------------------------------------------------------
 // Generic fallback: one warp per output row, weights read straight from global
 // memory in 4-byte words (any K % 8 == 0, rows 4-byte aligned), FP32 x in
-// shared memory.  Used for shapes the streaming plan does not cover.
+// shared memory.  Used for shapes the row-streaming kernel does not cover.
 // ---------------------------------------------------------------------------
 template <typename ST>
 __global__ void __launch_bounds__(256) gemv_simple_kernel(const __grid_constant__ GemvArgs a) {
@@ -528,7 +736,7 @@ __global__ void __launch_bounds__(256) gemv_simple_kernel(const __grid_constant_
       }
       acc[m] = warp_sum(sum);
     }
-    if (lane == 0) gemv_epilogue(sg, r, acc[0], acc[1], am_best);
+    if (lane == 0) am_best = gemv_epilogue(sg, r, acc[0], acc[1], am_best);
   }
   if (a.am_ws) argmax_finish(a, am_best, misc + 32);
 }

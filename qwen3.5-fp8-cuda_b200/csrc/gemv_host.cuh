@@ -25,62 +25,9 @@ static inline int sm_count() {
   return g_dev[d].sms;
 }
 
-// Shared memory budget of one streaming CTA: two CTAs (this kernel's and the
-// next kernel's, overlapped through programmatic dependent launch) fit in
-// one SM's 228 KB.
-constexpr int GEMV_SMEM_BUDGET = 104 * 1024;
-constexpr int GEMV_STAGE_TARGET = 32 * 1024;
-// Chunks per lane held in registers: above 6 the x slice no longer fits the
-// 113-register budget of two co-resident CTAs, so larger K splits into slices.
-constexpr int GEMV_MAX_J = 6;
-
-struct GemvPlan {
-  bool stream = false;
-  int nc = 8, j = 0, nslice = 1, npart = 1, rs = 1, nstages = 0, stage_bytes = 0, smem = 0, grid = 0;
-};
-
-// Streaming plan for a given K: K = 512 * J * nslice with J <= 8, nslice
-// dividing the consumer warp count, tiles of rs rows that never cross a
-// 128-row scale block.
-static inline bool plan_stream(int K, bool paired, GemvPlan& p) {
-  if (K <= 0 || K % 512 != 0) return false;
-  const int L = K / 512;
-  const int pair = paired ? 2 : 1;
-  struct Opt { int nc, nslice; };
-  const Opt opts[] = {{8, 1}, {8, 2}, {8, 4}, {6, 3}, {6, 6}};
-  for (const Opt& o : opts) {
-    if (L % o.nslice) continue;
-    const int J = L / o.nslice;
-    if (J > GEMV_MAX_J) continue;
-    if (o.nc == 6 && J != 6 && J != 3) continue;  // instantiated (6, J) kernels
-    const int npart = o.nslice * pair;
-    if (o.nc % npart) continue;
-    int rs = o.nc / npart;  // one item per warp per stage
-    if (rs & (rs - 1)) continue;
-    while (rs * 2 <= 128 && rs * 2 * K * pair <= GEMV_STAGE_TARGET / 2) rs *= 2;
-    const int sb = rs * K * pair;
-    if (sb > GEMV_SMEM_BUDGET / 2) continue;
-    int ns = 2;
-    while (ns < 8 && gemv_smem_layout(K, ns + 1, sb, rs, npart).total <= GEMV_SMEM_BUDGET) ++ns;
-    const GemvSmem L2 = gemv_smem_layout(K, ns, sb, rs, npart);
-    if (L2.total > 227 * 1024) continue;
-    p.stream = true;
-    p.nc = o.nc;
-    p.j = J;
-    p.nslice = o.nslice;
-    p.npart = npart;
-    p.rs = rs;
-    p.nstages = ns;
-    p.stage_bytes = sb;
-    p.smem = L2.total;
-    return true;
-  }
-  return false;
-}
-
-template <typename ST, int NC, int J>
-static cudaError_t launch_stream_inst(const GemvArgs& a, const GemvPlan& p, cudaStream_t st, bool pdl) {
-  auto kern = gemv_stream_kernel<ST, NC, J>;
+template <typename ST, bool PAIR>
+static cudaError_t launch_mma_inst(const GemvArgs& a, int grid, int smem, cudaStream_t st, bool pdl) {
+  auto kern = gemv_mma_kernel<ST, PAIR>;
   static bool attr_done[64] = {};
   const int d = current_device();
   if (!attr_done[d]) {
@@ -89,9 +36,9 @@ static cudaError_t launch_stream_inst(const GemvArgs& a, const GemvPlan& p, cuda
     attr_done[d] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.grid);
-  cfg.blockDim = dim3((NC + 1) * 32);
-  cfg.dynamicSmemBytes = p.smem;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GEMV_THREADS);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -99,26 +46,6 @@ static cudaError_t launch_stream_inst(const GemvArgs& a, const GemvPlan& p, cuda
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, a);
-}
-
-template <typename ST>
-static cudaError_t launch_stream(const GemvArgs& a, const GemvPlan& p, cudaStream_t st, bool pdl) {
-  if (p.nc == 8) {
-    switch (p.j) {
-      case 1: return launch_stream_inst<ST, 8, 1>(a, p, st, pdl);
-      case 2: return launch_stream_inst<ST, 8, 2>(a, p, st, pdl);
-      case 3: return launch_stream_inst<ST, 8, 3>(a, p, st, pdl);
-      case 4: return launch_stream_inst<ST, 8, 4>(a, p, st, pdl);
-      case 5: return launch_stream_inst<ST, 8, 5>(a, p, st, pdl);
-      case 6: return launch_stream_inst<ST, 8, 6>(a, p, st, pdl);
-    }
-  } else if (p.nc == 6) {
-    switch (p.j) {
-      case 3: return launch_stream_inst<ST, 6, 3>(a, p, st, pdl);
-      case 6: return launch_stream_inst<ST, 6, 6>(a, p, st, pdl);
-    }
-  }
-  return cudaErrorInvalidConfiguration;
 }
 
 template <typename ST>
@@ -159,41 +86,56 @@ static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t
 // Returns cudaErrorInvalidValue on bad arguments (nothing launched).
 static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool pdl, bool force_simple = false) {
   if (a.K <= 0 || a.K % 8 != 0 || a.nseg <= 0 || a.nseg > GEMV_MAX_SEG || !a.x) return cudaErrorInvalidValue;
-  bool paired = false, can_stream = aligned16(a.x) && !force_simple;
-  int ntiles = 0;
+  // Tensor-core path: K a multiple of 128, 16-byte aligned weights, and
+  // either every segment a gate/up pair or none.
+  bool mma_ok = a.K % 128 == 0 && !force_simple && aligned16(a.x) && (!a.x2 || aligned16(a.x2)) &&
+                (!a.h2_out || aligned16(a.h2_out)) && (!a.norm_w || aligned16(a.norm_w)) &&
+                (reinterpret_cast<uintptr_t>(a.xn_out) & 7u) == 0;
+  int npair = 0, nunits = 0, rows = 0;
   for (int s = 0; s < a.nseg; ++s) {
-    const GemvSeg& sg = a.seg[s];
+    GemvSeg& sg = a.seg[s];
     if (sg.n < 0 || !sg.w || !sg.s) return cudaErrorInvalidValue;
     if (sg.epi != EPI_ARGMAX && sg.n > 0 && !sg.y) return cudaErrorInvalidValue;
-    if (sg.epi == EPI_SILU_PAIR) {
-      if (!sg.w2 || !sg.s2) return cudaErrorInvalidValue;
-      paired = true;
-      if (!aligned16(sg.w2)) can_stream = false;
-    }
+    if (sg.epi == EPI_SILU_PAIR && (!sg.w2 || !sg.s2)) return cudaErrorInvalidValue;
     if (sg.epi == EPI_CONV && (sg.cw < 1 || sg.cw > 8 || !sg.aux0 || !sg.aux2)) return cudaErrorInvalidValue;
     if (sg.epi == EPI_ARGMAX && !a.am_ws) return cudaErrorInvalidValue;
-    if (!aligned16(sg.w)) can_stream = false;
+    if (!aligned16(sg.w) || (sg.epi == EPI_SILU_PAIR && !aligned16(sg.w2))) mma_ok = false;
+    if (sg.kblk <= 1 || sg.kblk != (a.K + 127) / 128) mma_ok = false;  // block scales only
+    npair += sg.epi == EPI_SILU_PAIR;
+    rows += sg.n;
   }
-  if (paired) {
-    for (int s = 0; s < a.nseg; ++s)
-      if (a.seg[s].epi != EPI_SILU_PAIR) can_stream = false;  // one tile shape per launch
-  }
-  GemvPlan p;
-  if (can_stream && plan_stream(a.K, paired, p)) {
+  if (rows == 0) return cudaSuccess;
+  if (npair != 0 && npair != a.nseg) mma_ok = false;
+  if (mma_ok && (a.K / 128 + GEMV_WARPS - 1) / GEMV_WARPS > 32) mma_ok = false;  // K > 32768
+  if (mma_ok) {
+    // Work units: 8 rows of a gate/up pair, else 16 rows of one matrix.
+    const bool pair = npair != 0;
+    const int unit_rows = pair ? GEMV_TILE : 2 * GEMV_TILE;
     for (int s = 0; s < a.nseg; ++s) {
-      a.seg[s].tile0 = ntiles;
-      ntiles += (a.seg[s].n + p.rs - 1) / p.rs;
+      a.seg[s].unit0 = nunits;
+      nunits += (a.seg[s].n + unit_rows - 1) / unit_rows;
     }
-    if (ntiles == 0) return cudaSuccess;
-    a.ntiles = ntiles;
-    a.rs = p.rs;
-    a.npart = p.npart;
-    a.nslice = p.nslice;
-    a.nstages = p.nstages;
-    a.stage_bytes = p.stage_bytes;
-    const int sms = sm_count();
-    p.grid = ntiles < sms ? ntiles : sms;
-    return f32_scales ? launch_stream<float>(a, p, st, pdl) : launch_stream<bf16>(a, p, st, pdl);
+    a.nunits = nunits;
+    // Split K over S warps of a CTA when there are too few units to give
+    // every resident warp one; a warp holds the scales of at most 32 K-blocks
+    // (one per lane).
+    const int nkb = a.K / 128;
+    const int warps = sm_count() * GEMV_CTAS_PER_SM * GEMV_WARPS;
+    int S = 1;
+    while (S < GEMV_WARPS && (long long)nunits * S < warps && 2 * S <= nkb) S *= 2;
+    while (S < GEMV_WARPS && (nkb + S - 1) / S > 32) S *= 2;
+    a.nslice = S;
+    const int smem = gemv_smem_layout(a.K).total;
+    if (smem > 227 * 1024) return cudaErrorInvalidValue;
+    const int cap = sm_count() * GEMV_CTAS_PER_SM;
+    const int groups = GEMV_WARPS / S;
+    int grid = (nunits + groups - 1) / groups;
+    grid = grid < cap ? grid : cap;
+    if (pair)
+      return f32_scales ? launch_mma_inst<float, true>(a, grid, smem, st, pdl)
+                        : launch_mma_inst<bf16, true>(a, grid, smem, st, pdl);
+    return f32_scales ? launch_mma_inst<float, false>(a, grid, smem, st, pdl)
+                      : launch_mma_inst<bf16, false>(a, grid, smem, st, pdl);
   }
   return f32_scales ? launch_simple<float>(a, st, pdl) : launch_simple<bf16>(a, st, pdl);
 }

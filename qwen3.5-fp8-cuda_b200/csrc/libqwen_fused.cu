@@ -22,6 +22,15 @@ namespace {
 
 thread_local int g_last_error = 0;
 int g_pdl_enabled = 1;
+// Regions the next engine launch on this host thread prefetches into L2
+// (set by qwen_set_prefetch, consumed and cleared by that launch).
+thread_local L2Prefetch g_next_pf = {};
+
+inline L2Prefetch take_prefetch() {
+  L2Prefetch pf = g_next_pf;
+  g_next_pf = L2Prefetch{};
+  return pf;
+}
 
 inline int record(cudaError_t e) {
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -93,6 +102,20 @@ int qwen_get_device_error(unsigned int* out) {
 }
 
 void qwen_set_pdl(int enable) { g_pdl_enabled = enable; }
+
+// Weight regions (up to four; null / 0 entries ignored) that the next engine
+// launch issued on this host thread pulls into L2 while it runs -- normally
+// the weights of the launch after it.  Sizes are rounded down to 16 bytes.
+void qwen_set_prefetch(const void* p0, unsigned long long n0, const void* p1, unsigned long long n1,
+                       const void* p2, unsigned long long n2, const void* p3, unsigned long long n3) {
+  const void* p[4] = {p0, p1, p2, p3};
+  const unsigned long long n[4] = {n0, n1, n2, n3};
+  for (int i = 0; i < 4; ++i) {
+    const bool ok = p[i] && (reinterpret_cast<uintptr_t>(p[i]) & 15u) == 0;
+    g_next_pf.p[i] = ok ? p[i] : nullptr;
+    g_next_pf.n[i] = ok ? (n[i] & ~15ull) : 0ull;
+  }
+}
 
 int qwen_abi_version(void) { return 1; }
 
@@ -352,6 +375,7 @@ int launch_lm_head_argmax(const void* x, const float* norm_w, float eps, const v
   a.am_key_out = key_out;
   a.am_token_out = token_out;
   a.pos_inc = pos_inc;
+  a.pf = take_prefetch();
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -393,6 +417,7 @@ int qwen_attn_in_proj(const void* hidden, const float* norm_w, float eps, const 
   a.seg[0] = seg(w_q, s_q, q_out, N_q, K_blk);
   a.seg[1] = seg(w_k, s_k, k_out, N_k, K_blk);
   a.seg[2] = seg(w_v, s_v, v_out, N_v, K_blk);
+  a.pf = take_prefetch();
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -419,6 +444,7 @@ int qwen_gdn_in_proj(const void* hidden, const float* norm_w, float eps, int K, 
   a.seg[2].aux0 = A_log;
   a.seg[2].aux1 = dt_bias;
   a.seg[3] = seg(w_b, s_b, beta_out, N_heads, K_blk, EPI_GATE_BETA);
+  a.pf = take_prefetch();
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -442,6 +468,7 @@ int qwen_gdn_decode(const void* qkv, const float* g, const void* beta, float* st
   a.eps = eps;
   a.rep = n_v_heads / n_k_heads;
   a.gated = 1;
+  a.pf = take_prefetch();
   return record(launch_gdn(a, n_v_heads, head_dim, stream, engine_pdl()));
 }
 
@@ -452,6 +479,7 @@ int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K,
   a.nseg = 1;
   a.seg[0] = seg(w, s, y, N, K_blk, EPI_RESID);
   a.seg[0].aux0 = res;
+  a.pf = take_prefetch();
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -466,6 +494,7 @@ int qwen_mlp_gate_up(const void* h2, const float* norm_w, float eps, const void*
   a.seg[0] = seg(w_g, s_g, silu_out, N, K_blk, EPI_SILU_PAIR);
   a.seg[0].w2 = static_cast<const uint8_t*>(w_u);
   a.seg[0].s2 = s_u;
+  a.pf = take_prefetch();
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -501,6 +530,7 @@ int qwen_attn_decode(const void* q_all, const void* k_new, const void* v_new, co
   a.ws_part = ws_part;
   a.ws_count = ws_count;
   a.out = static_cast<bf16*>(out);
+  a.pf = take_prefetch();
   if (!pos || (long long)chunk * nsplit < max_seq) return record(cudaErrorInvalidValue);
   return record(launch_attn(a, head_dim, stream, engine_pdl()));
 }

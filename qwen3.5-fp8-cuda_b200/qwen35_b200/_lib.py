@@ -51,6 +51,8 @@ NEW_FUSED = {
     "qwen_last_error": (I, []),
     "qwen_get_device_error": (I, [P]),
     "qwen_set_pdl": (None, [I]),
+    "qwen_set_prefetch": (None, [P, ctypes.c_ulonglong, P, ctypes.c_ulonglong, P, ctypes.c_ulonglong, P,
+                                 ctypes.c_ulonglong]),
     "qwen_abi_version": (I, []),
     "launch_gemv_f32s": (I, [P, P, P, P, I, I, I, P]),
     "qwen_gemv_generic": (I, [P, P, P, I, P, I, I, I, P]),

@@ -50,8 +50,9 @@ class Qwen35DecodeEngine:
     """Greedy batch-1 decoder over device-resident weights (see ``weights.py``)."""
 
     def __init__(self, cfg, weights, max_seq: int = 4096, device="cuda", keep_logits: bool = False,
-                 attn_chunk: int | None = None):
+                 attn_chunk: int | None = None, prefetch: bool = True):
         self.cfg = cfg
+        self.prefetch = prefetch
         self.w = weights
         self.max_seq = int(max_seq)
         self.device = torch.device(device)
@@ -118,63 +119,98 @@ class Qwen35DecodeEngine:
             t.zero_()
         self.pos.zero_()
 
-    def _launch_step(self, stream):
+    # Bytes of one region a launch may prefetch into L2 for its successor.
+    PREFETCH_CAP = 64 << 20
+
+    def _regions(self, *tensors):
+        """(pointer, bytes) of the tensors a launch streams, for L2 look-ahead."""
+        out = []
+        for t in tensors:
+            if t is None:
+                continue
+            out.append((t.data_ptr(), min(t.numel() * t.element_size(), self.PREFETCH_CAP)))
+        return out[:4]
+
+    def _plan_step(self):
+        """The decode step as a list of (launch(stream), regions it streams)."""
         cfg, lib, w = self.cfg, self.lib, self.w
         H, I = cfg.hidden_size, cfg.intermediate_size
         eps = cfg.rms_norm_eps
-        st = P(stream)
-        n = 0
+        plan = []
 
         def chk(status, what):
             _lib.check(status, what)
 
-        chk(lib.qwen_embed(_p(w["embed"]), _p(self.token), _p(self.hidden), H, st), "qwen_embed")
-        n += 1
+        plan.append((lambda st: chk(lib.qwen_embed(_p(w["embed"]), _p(self.token), _p(self.hidden), H, st),
+                                    "qwen_embed"), []))
         for i, ly in enumerate(w["layers"]):
             if cfg.layer_types[i] == "full_attention":
                 (wq, sq), (wk, sk), (wv, sv), (wo, so) = ly["q_proj"], ly["k_proj"], ly["v_proj"], ly["o_proj"]
-                chk(lib.qwen_attn_in_proj(_p(self.hidden), _p(ly["input_layernorm"]), eps,
-                                          _p(wq), _p(sq), wq.shape[0], _p(wk), _p(sk), wk.shape[0],
-                                          _p(wv), _p(sv), wv.shape[0], H, scale_mode(wq.shape[0], sq),
-                                          _p(self.q_all), _p(self.k_new), _p(self.v_new), st), "attn_in_proj")
-                chk(lib.qwen_attn_decode(_p(self.q_all), _p(self.k_new), _p(self.v_new), _p(ly["q_norm"]),
-                                         _p(ly["k_norm"]), _p(self.cos), _p(self.sin), _p(self.k_cache[i]),
-                                         _p(self.v_cache[i]), _p(self.pos), self.max_seq,
-                                         cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim,
-                                         cfg.rotary_dim, eps, self.attn_chunk, self.attn_nsplit,
-                                         _p(self.attn_ws), _p(self.attn_cnt), _p(self.attn_out), st), "attn_decode")
-                chk(lib.qwen_linear_resid(_p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1],
-                                          scale_mode(wo.shape[0], so), _p(self.hidden), _p(self.h2), st), "o_proj")
+                plan.append((lambda st, ly=ly, wq=wq, sq=sq, wk=wk, sk=sk, wv=wv, sv=sv: chk(lib.qwen_attn_in_proj(
+                    _p(self.hidden), _p(ly["input_layernorm"]), eps, _p(wq), _p(sq), wq.shape[0], _p(wk), _p(sk),
+                    wk.shape[0], _p(wv), _p(sv), wv.shape[0], H, scale_mode(wq.shape[0], sq), _p(self.q_all),
+                    _p(self.k_new), _p(self.v_new), st), "attn_in_proj"), self._regions(wq, wk, wv)))
+                plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_attn_decode(
+                    _p(self.q_all), _p(self.k_new), _p(self.v_new), _p(ly["q_norm"]), _p(ly["k_norm"]),
+                    _p(self.cos), _p(self.sin), _p(self.k_cache[i]), _p(self.v_cache[i]), _p(self.pos),
+                    self.max_seq, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim, cfg.rotary_dim, eps,
+                    self.attn_chunk, self.attn_nsplit, _p(self.attn_ws), _p(self.attn_cnt), _p(self.attn_out), st),
+                    "attn_decode"), self._regions(self.k_cache[i], self.v_cache[i])))
+                plan.append((lambda st, wo=wo, so=so: chk(lib.qwen_linear_resid(
+                    _p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
+                    _p(self.hidden), _p(self.h2), st), "o_proj"), self._regions(wo)))
             else:
                 (wqkv, sqkv), (wz, sz) = ly["in_proj_qkv"], ly["in_proj_z"]
                 (wa, sa), (wb, sb), (wo, so) = ly["in_proj_a"], ly["in_proj_b"], ly["out_proj"]
-                chk(lib.qwen_gdn_in_proj(_p(self.hidden), _p(ly["input_layernorm"]), eps, H,
-                                         scale_mode(wqkv.shape[0], sqkv), _p(wqkv), _p(sqkv), wqkv.shape[0],
-                                         _p(ly["conv1d_w"]), _p(self.conv_state[i]), cfg.linear_conv_kernel_dim,
-                                         _p(self.qkv_conv), _p(wz), _p(sz), wz.shape[0], _p(self.z),
-                                         _p(wa), _p(sa), _p(wb), _p(sb), wa.shape[0], _p(ly["A_log"]),
-                                         _p(ly["dt_bias"]), _p(self.g), _p(self.beta), st), "gdn_in_proj")
-                chk(lib.qwen_gdn_decode(_p(self.qkv_conv), _p(self.g), _p(self.beta), _p(self.state[i]),
-                                        _p(self.z), _p(ly["norm_w"]), eps, _p(self.attn_out),
-                                        cfg.linear_num_key_heads, cfg.linear_num_value_heads,
-                                        cfg.linear_value_head_dim, st), "gdn_decode")
-                chk(lib.qwen_linear_resid(_p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1],
-                                          scale_mode(wo.shape[0], so), _p(self.hidden), _p(self.h2), st),
-                    "out_proj")
+                plan.append((lambda st, ly=ly, i=i, wqkv=wqkv, sqkv=sqkv, wz=wz, sz=sz, wa=wa, sa=sa, wb=wb, sb=sb:
+                             chk(lib.qwen_gdn_in_proj(
+                                 _p(self.hidden), _p(ly["input_layernorm"]), eps, H, scale_mode(wqkv.shape[0], sqkv),
+                                 _p(wqkv), _p(sqkv), wqkv.shape[0], _p(ly["conv1d_w"]), _p(self.conv_state[i]),
+                                 cfg.linear_conv_kernel_dim, _p(self.qkv_conv), _p(wz), _p(sz), wz.shape[0],
+                                 _p(self.z), _p(wa), _p(sa), _p(wb), _p(sb), wa.shape[0], _p(ly["A_log"]),
+                                 _p(ly["dt_bias"]), _p(self.g), _p(self.beta), st), "gdn_in_proj"),
+                             self._regions(wqkv, wz, wa, wb)))
+                plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_gdn_decode(
+                    _p(self.qkv_conv), _p(self.g), _p(self.beta), _p(self.state[i]), _p(self.z), _p(ly["norm_w"]),
+                    eps, _p(self.attn_out), cfg.linear_num_key_heads, cfg.linear_num_value_heads,
+                    cfg.linear_value_head_dim, st), "gdn_decode"), self._regions(self.state[i])))
+                plan.append((lambda st, wo=wo, so=so: chk(lib.qwen_linear_resid(
+                    _p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
+                    _p(self.hidden), _p(self.h2), st), "out_proj"), self._regions(wo)))
             (wg, sg), (wu, su), (wd, sd) = ly["gate_proj"], ly["up_proj"], ly["down_proj"]
-            chk(lib.qwen_mlp_gate_up(_p(self.h2), _p(ly["post_attention_layernorm"]), eps, _p(wg), _p(sg),
-                                     _p(wu), _p(su), I, H, scale_mode(I, sg), _p(self.silu), st), "gate_up")
-            chk(lib.qwen_linear_resid(_p(self.silu), _p(wd), _p(sd), H, I, scale_mode(H, sd), _p(self.h2),
-                                      _p(self.hidden), st), "down")
-            n += 5
+            plan.append((lambda st, ly=ly, wg=wg, sg=sg, wu=wu, su=su: chk(lib.qwen_mlp_gate_up(
+                _p(self.h2), _p(ly["post_attention_layernorm"]), eps, _p(wg), _p(sg), _p(wu), _p(su), I, H,
+                scale_mode(I, sg), _p(self.silu), st), "gate_up"), self._regions(wg, wu)))
+            plan.append((lambda st, wd=wd, sd=sd: chk(lib.qwen_linear_resid(
+                _p(self.silu), _p(wd), _p(sd), H, I, scale_mode(H, sd), _p(self.h2), _p(self.hidden), st), "down"),
+                self._regions(wd)))
         head = w["lm_head"]
         if not isinstance(head, tuple):
             raise NotImplementedError("BF16 LM head: use an FP8 head (cfg.fp8_lm_head=True)")
         wh, sh = head
-        chk(lib.launch_lm_head_argmax(_p(self.hidden), _p(w["norm_f"]), eps, _p(wh), _p(sh), wh.shape[0], H,
-                                      scale_mode(wh.shape[0], sh), 0, _p(self.am_ws), _p(self.key), _p(self.token),
-                                      _p(self.logits), _p(self.pos), st), "lm_head_argmax")
-        n += 1
+        plan.append((lambda st: chk(lib.launch_lm_head_argmax(
+            _p(self.hidden), _p(w["norm_f"]), eps, _p(wh), _p(sh), wh.shape[0], H, scale_mode(wh.shape[0], sh), 0,
+            _p(self.am_ws), _p(self.key), _p(self.token), _p(self.logits), _p(self.pos), st), "lm_head_argmax"),
+            self._regions(wh)))
+        return plan
+
+    def _launch_step(self, stream):
+        """Issue one decode step; every launch prefetches its successor's regions."""
+        plan = self._plan_step()
+        st = P(stream)
+        n = len(plan)
+        for j, (launch, _) in enumerate(plan):
+            if self.prefetch:
+                nxt = []
+                k = (j + 1) % n
+                while not nxt and k != j:
+                    nxt = plan[k][1]
+                    k = (k + 1) % n
+                args = []
+                for ptr, nbytes in (nxt + [(0, 0)] * 4)[:4]:
+                    args += [P(ptr), nbytes]
+                self.lib.qwen_set_prefetch(*args)
+            launch(st)
         self.launches_per_step = n
 
     # ------------------------------------------------------------------
