@@ -97,7 +97,8 @@ struct GemvArgs {
   int pro;
   int nseg;
   int nunits;          // total work units (filled by the planner)
-  int nslice;          // warps sharing one tile (K split), divides GEMV_WARPS
+  int nslice;          // K split: warps sharing one unit (streaming kernel) or CTAs (tensor-core kernel)
+  int stages;          // tensor-core kernel: weight stages in the shared-memory ring
   unsigned long long* am_ws;       // ARGMAX workspace {key, count}: zero before first use, left zeroed
   unsigned long long* am_key_out;  // optional: final packed key
   long long* am_token_out;         // optional: final token id

@@ -2,8 +2,14 @@
 #pragma once
 
 #include "gemv.cuh"
+#include "gemv_tc.cuh"
 
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
 #include <cstring>
+#include <mutex>
+#include <unordered_map>
 
 namespace qwen {
 
@@ -82,6 +88,179 @@ static cudaError_t launch_simple(const GemvArgs& a, cudaStream_t st, bool pdl) {
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// GEMV path selection: 0 = tcgen05 (default), 1 = mma.sync streaming kernel.
+// QWEN_GEMV_PATH=mma in the environment selects the latter (for comparison).
+static inline int gemv_path() {
+  static int path = -1;
+  if (path < 0) {
+    const char* e = getenv("QWEN_GEMV_PATH");
+    path = (e && std::strcmp(e, "mma") == 0) ? 1 : 0;
+  }
+  return path;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core (tcgen05 + TMA) path
+// ---------------------------------------------------------------------------
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// Tensor map of an [rows, K] E4M3 matrix: boxes of 128 rows x 128 bytes,
+// 128-byte swizzle, rows past the end read as zero.  Cached per (matrix,
+// rows, K).
+static bool weight_tmap(CUtensorMap* out, const void* w, int rows, int K) {
+  struct Key {
+    const void* w;
+    int rows, K;
+    bool operator==(const Key& o) const { return w == o.w && rows == o.rows && K == o.K; }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.w) ^ ((size_t)k.rows * 0x9E3779B97F4A7C15ull) ^ (size_t)k.K;
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, CUtensorMap, Hash> cache;
+  const Key key{w, rows, K};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tmap_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K};
+  cuuint32_t box[2] = {128, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMap m;
+  if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, m);
+  *out = m;
+  return true;
+}
+
+template <typename ST, bool PAIR>
+static cudaError_t launch_tc_inst(const GemvArgs& a, const GemvMaps& m, int grid, int smem, cudaStream_t st,
+                                  bool pdl) {
+  auto kern = gemv_tc_kernel<ST, PAIR>;
+  static bool attr_done[64] = {};
+  const int d = current_device();
+  if (!attr_done[d]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    attr_done[d] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a, m);
+}
+
+// Plans and launches the tensor-core path.  Returns cudaErrorNotSupported
+// (nothing launched) when the launch is not eligible for it: K not a
+// multiple of 128 (or below 256), scales not in 128x128 block layout,
+// misaligned buffers, or mixed paired and unpaired segments.
+static cudaError_t gemv_tc_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool pdl) {
+  const int K = a.K;
+  if (K % 128 != 0 || K < 256) return cudaErrorNotSupported;
+  const int nkb = K / 128;
+  if (!aligned16(a.x) || (a.x2 && !aligned16(a.x2)) || (a.h2_out && !aligned16(a.h2_out)) ||
+      (a.norm_w && !aligned16(a.norm_w)) || (reinterpret_cast<uintptr_t>(a.xn_out) & 7u) != 0)
+    return cudaErrorNotSupported;
+  int npair = 0;
+  for (int s = 0; s < a.nseg; ++s) {
+    const GemvSeg& sg = a.seg[s];
+    if (sg.kblk != nkb || !aligned16(sg.w)) return cudaErrorNotSupported;  // block scales only
+    if (sg.epi == EPI_SILU_PAIR) {
+      if (!aligned16(sg.w2)) return cudaErrorNotSupported;
+      ++npair;
+    }
+  }
+  if (npair != 0 && npair != a.nseg) return cudaErrorNotSupported;
+  const bool pair = npair != 0;
+  const int P = pair ? 2 : 1;
+  GemvMaps m;
+  std::memset(&m, 0, sizeof(m));
+  int nunits = 0;
+  for (int s = 0; s < a.nseg; ++s) {
+    GemvSeg& sg = a.seg[s];
+    sg.unit0 = nunits;
+    nunits += (sg.n + TC_ROWS - 1) / TC_ROWS;
+    if (sg.n > 0) {
+      if (!weight_tmap(&m.map[s][0], sg.w, sg.n, K)) return cudaErrorNotSupported;
+      if (pair && !weight_tmap(&m.map[s][1], sg.w2, sg.n, K)) return cudaErrorNotSupported;
+    }
+  }
+  a.nunits = nunits;
+  // K split C: at most 32 K-blocks per item (the epilogue keeps one scale per
+  // lane); otherwise the C that minimises the work of the busiest CTA,
+  // counting about two K-blocks of fixed cost per item and the partial-sum
+  // reduction that a split adds.  The grid is a multiple of C so that each
+  // CTA keeps one K slice.
+  const int sms = sm_count();
+  int best_c = 0;
+  double best_cost = 0;
+  const int cmin = (nkb + 31) / 32;
+  for (int c = cmin; c <= nkb && c <= 64 && c <= sms; ++c) {
+    const long long items = (long long)nunits * c;
+    if (c > 1 && (items * P * TC_ROWS > TC_PART_FLOATS || nunits > TC_MAX_CNT)) break;
+    const long long slots = (long long)(sms / c) * c;
+    const long long waves = (items + slots - 1) / slots;
+    const double cost = (double)waves * ((nkb + c - 1) / c + 2) + (c > 1 ? 1.0 + c / 8.0 : 0.0);
+    if (best_c == 0 || cost < best_cost) {
+      best_c = c;
+      best_cost = cost;
+    }
+  }
+  if (best_c == 0) return cudaErrorNotSupported;
+  a.nslice = best_c;
+  const long long items = (long long)nunits * best_c;
+  const long long slots = (long long)(sms / best_c) * best_c;
+  const int grid = (int)(items < slots ? items : slots);
+  // Launches that stream for several waves get the whole shared memory; the
+  // others stay within half of it (see gemv_tc.cuh).  The deepest ring that
+  // fits streams best: under full load the HBM round trip is several us.
+  const int budget = items >= 2 * slots ? TC_SMEM_MAX : TC_SMEM_SHARED;
+  int S = tc_stages_for(K, P, best_c, budget);
+  if (S == 0) S = tc_stages_for(K, P, best_c, TC_SMEM_MAX);
+  if (S == 0) return cudaErrorNotSupported;
+  a.stages = S;
+  const TcSmem L = tc_smem_layout(K, P, best_c, S);
+  if (pair)
+    return f32_scales ? launch_tc_inst<float, true>(a, m, grid, L.total, st, pdl)
+                      : launch_tc_inst<bf16, true>(a, m, grid, L.total, st, pdl);
+  return f32_scales ? launch_tc_inst<float, false>(a, m, grid, L.total, st, pdl)
+                    : launch_tc_inst<bf16, false>(a, m, grid, L.total, st, pdl);
+}
+
 // Validate, plan and launch.  `f32_scales` selects FP32 scale storage.
 // Returns cudaErrorInvalidValue on bad arguments (nothing launched).
 static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool pdl, bool force_simple = false) {
@@ -105,6 +284,10 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
     rows += sg.n;
   }
   if (rows == 0) return cudaSuccess;
+  if (!force_simple && gemv_path() == 0) {
+    const cudaError_t e = gemv_tc_run(a, f32_scales, st, pdl);
+    if (e != cudaErrorNotSupported) return e;
+  }
   if (npair != 0 && npair != a.nseg) mma_ok = false;
   if (mma_ok && (a.K / 128 + GEMV_WARPS - 1) / GEMV_WARPS > 32) mma_ok = false;  // K > 32768
   if (mma_ok) {
