@@ -143,6 +143,15 @@ int qwen_gdn_decode(const void* qkv, const float* g, const void* beta, float* st
 /* y = bf16(res + bf16(W x)): o_proj / out_proj / down with the residual add (553-559). */
 int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K, int K_blk, const void* res, void* y,
                       cudaStream_t stream);
+/* Tensor parallelism (row/column sharding of the decode step across GPUs;
+ * the reference has no multi-GPU path, these replace nothing):
+ * y_f32 = this rank's partial GEMV over its slice of K, to be all-reduced. */
+int qwen_linear_partial(const void* x, const void* w, const void* s, int N, int K, int K_blk, float* y,
+                        cudaStream_t stream);
+/* y = bf16(res + bf16(v)) for n elements, v the all-reduced partial sums. */
+int qwen_resid_add_f32(const void* res, const float* v, void* y, int n, cudaStream_t stream);
+/* token = the greedy token id encoded in an all-reduced packed argmax key. */
+int qwen_token_from_key(const long long* key, long long* token, cudaStream_t stream);
 /* silu_out = bf16(silu(g)*u), g/u = GEMVs of RMSNorm(h2) (398-479, 1173-1190). */
 int qwen_mlp_gate_up(const void* h2, const float* norm_w, float eps, const void* w_g, const void* s_g,
                      const void* w_u, const void* s_u, int N, int K, int K_blk, void* silu_out, cudaStream_t stream);

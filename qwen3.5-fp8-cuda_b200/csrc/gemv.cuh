@@ -58,6 +58,7 @@ enum GemvEpi : int {
   EPI_CONV = 4,       // y[r] = bf16(silu(bf16(conv(state[r,1:], bf16(v))))); state updated
   EPI_GATE_G = 5,     // y(f32)[r] = -exp(A_log[r]) * softplus(bf16(v) + dt_bias[r])
   EPI_GATE_BETA = 6,  // y[r] = bf16(sigmoid(bf16(v)))
+  EPI_F32 = 7,        // y(f32)[r] = v (partial sums of a K-sliced tensor-parallel GEMV)
 };
 
 enum GemvPro : int {
@@ -204,6 +205,9 @@ __device__ __noinline__ unsigned long long gemv_epilogue(const GemvSeg& sg, int 
       float b = bfround(v);
       reinterpret_cast<bf16*>(sg.y)[r] = f2bf(1.0f / (1.0f + expf(-b)));
     } break;
+    case EPI_F32:
+      reinterpret_cast<float*>(sg.y)[r] = v;
+      break;
     default:
       break;
   }

@@ -483,6 +483,50 @@ int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K,
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
+// Tensor parallelism, K-sliced projection: y_f32 = partial GEMV over this
+// rank's slice of K (the caller all-reduces y_f32 and then applies
+// qwen_resid_add_f32).
+int qwen_linear_partial(const void* x, const void* w, const void* s, int N, int K, int K_blk, float* y,
+                        cudaStream_t stream) {
+  GemvArgs a = make_args(x, K);
+  a.nseg = 1;
+  a.seg[0] = seg(w, s, y, N, K_blk, EPI_F32);
+  a.pf = take_prefetch();
+  return record(gemv_run(a, false, stream, engine_pdl()));
+}
+
+// y = bf16(res + bf16(v)) for n elements (v: all-reduced FP32 partial sums).
+int qwen_resid_add_f32(const void* res, const float* v, void* y, int n, cudaStream_t stream) {
+  if (n <= 0 || !res || !v || !y) return record(cudaErrorInvalidValue);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((n + 255) / 256);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = engine_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return record(cudaLaunchKernelEx(&cfg, resid_add_f32_kernel, static_cast<const bf16*>(res), v,
+                                   static_cast<bf16*>(y), n));
+}
+
+// token = greedy token encoded in an all-reduced packed argmax key.
+int qwen_token_from_key(const long long* key, long long* token, cudaStream_t stream) {
+  if (!key || !token) return record(cudaErrorInvalidValue);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = engine_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return record(cudaLaunchKernelEx(&cfg, token_from_key_kernel, reinterpret_cast<const unsigned long long*>(key),
+                                   token));
+}
+
 // silu_out = bf16(silu(g) * u) with g, u = GEMV(RMSNorm(1+w)(h2)).
 int qwen_mlp_gate_up(const void* h2, const float* norm_w, float eps, const void* w_g, const void* s_g,
                      const void* w_u, const void* s_u, int N, int K, int K_blk, void* silu_out, cudaStream_t stream) {

@@ -90,4 +90,22 @@ static inline cudaError_t launch_add(const void* a, const void* b, void* out, in
   return cudaGetLastError();
 }
 
+// Tensor-parallel helpers.
+// y = bf16(res + bf16(v)) from the all-reduced FP32 partial sums v of a
+// K-sliced projection: the residual epilogue of qwen_linear_resid applied
+// after the reduction.
+__global__ void resid_add_f32_kernel(const bf16* __restrict__ res, const float* __restrict__ v, bf16* __restrict__ y,
+                                     int n) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = f2bf(bf2f(res[i]) + bfround(v[i]));
+}
+// token = index part of the all-reduced packed argmax key.
+__global__ void token_from_key_kernel(const unsigned long long* key, long long* token) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
+  *token = (long long)(0xffffffffu - (uint32_t)(*key & 0xffffffffull));
+}
+
 }  // namespace qwen

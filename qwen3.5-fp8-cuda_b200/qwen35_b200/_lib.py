@@ -65,6 +65,9 @@ NEW_FUSED = {
     "qwen_mlp_gate_up": (I, [P, P, F, P, P, P, P, I, I, I, P, P]),
     "qwen_attn_decode": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, I, I, P, P, P, P]),
     "qwen_attn_decode_noalloc": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, I, I, P, P]),
+    "qwen_linear_partial": (I, [P, P, P, I, I, I, P, P]),
+    "qwen_resid_add_f32": (I, [P, P, P, I, P]),
+    "qwen_token_from_key": (I, [P, P, P]),
 }
 NEW_FP8 = {
     "qwen_fp8_last_error": (I, []),

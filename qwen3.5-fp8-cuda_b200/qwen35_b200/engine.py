@@ -109,6 +109,7 @@ class Qwen35DecodeEngine:
         self._h_tok = torch.zeros(1, dtype=torch.int64, pin_memory=True)
         self._h_out = torch.zeros(1, dtype=torch.int64, pin_memory=True)
         self.launches_per_step = 0
+        self.kernels_per_step = 0
 
     # ------------------------------------------------------------------
     def reset(self):
@@ -212,6 +213,7 @@ class Qwen35DecodeEngine:
                 self.lib.qwen_set_prefetch(*args)
             launch(st)
         self.launches_per_step = n
+        self.kernels_per_step = n - getattr(self, "collectives_per_step", 0)
 
     # ------------------------------------------------------------------
     def step_eager(self):
