@@ -14,9 +14,10 @@ than the 126 MB L2, so no flush is needed between steps.
 Keys beyond the base contract:
   e2e           the same K steps through the public API Qwen35DecodeEngine.decode()
                 (token H2D from pinned memory + graph + token D2H + sync per step)
-  roofline      the dominant kernel (gemv_tc_kernel, the tcgen05 + TMA GEMV with
-                the fused greedy argmax) timed alone on the LM-head launch of
-                config 2, back to back (burst peak)
+  roofline      the dominant kernel (gemv_tcw_kernel, the tcgen05 + TMA GEMV with
+                the weights as the N = 256 MMA operand and the fused greedy
+                argmax) timed alone on the LM-head launch of config 2, back to
+                back (burst peak)
   step_roofline algorithmic bytes of a whole decode step / device time per step
   cpu_baseline  the CPU oracle port (explicit FP8->FP32 dequant + torch matmul)
                 on a bounded sample of the step, scaled to tok/s
@@ -465,7 +466,7 @@ def run_ours(args):
         "gpu_launches": eng.kernels_per_step * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": load_traffic(),
-                     "kernel": "gemv_tc_kernel<bf16,false> (tcgen05 + TMA) on the LM head (248320x2560 E4M3, config 2)",
+                     "kernel": "gemv_tcw_kernel<bf16,false> (tcgen05 N=256 + TMA) on the LM head (248320x2560 E4M3, config 2)",
                      "bytes_per_launch": hb, "us_per_launch": round(head_s * 1e6, 2), "peak_kind": peak_kind},
         "step_roofline": {"bytes_per_step": sbytes, "achieved": round(sbytes / step_s / 1e9, 1),
                           "frac": round(sbytes / step_s / 1e9 / peak, 4), "unit": "GB/s"},

@@ -100,6 +100,10 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
   pdl_wait();
 
   const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_const;
+  if (pos < 0 || pos >= a.max_seq) {  // uniform over the grid: every CTA leaves
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) qwen_err_set(ERR_POS_RANGE);
+    return;
+  }
   const int total = a.seq_len > 0 ? a.seq_len : pos + 1;
   const float qscale = rsqrtf((float)D);
   const float* cs = a.prep && a.cos ? a.cos + (size_t)pos * a.rot : nullptr;

@@ -25,6 +25,7 @@ enum : unsigned {
   ERR_TIMEOUT_FULL = 1,     // consumer gave up waiting for a bulk copy
   ERR_TIMEOUT_EMPTY = 2,    // producer gave up waiting for a free stage
   ERR_TIMEOUT_DRAIN = 3,    // producer gave up waiting for its own copies
+  ERR_POS_RANGE = 5,        // a device-side cache position outside [0, max_seq)
 };
 
 // One error word per shared library (each library is a single translation

@@ -3,6 +3,7 @@
 
 #include "gemv.cuh"
 #include "gemv_tc.cuh"
+#include "gemv_tcw.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -88,15 +89,28 @@ static cudaError_t launch_simple(const GemvArgs& a, cudaStream_t st, bool pdl) {
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// GEMV path selection: 0 = tcgen05 (default), 1 = mma.sync streaming kernel.
-// QWEN_GEMV_PATH=mma in the environment selects the latter (for comparison).
+// GEMV path selection: 0 = tcgen05 with the weights as the N = 256 operand
+// (default, gemv_tcw.cuh), 1 = mma.sync streaming kernel, 2 = tcgen05 with
+// the weights as the M = 128 operand (gemv_tc.cuh).  QWEN_GEMV_PATH=mma or
+// =tc128 in the environment selects the others (for comparison).
 static inline int gemv_path() {
   static int path = -1;
   if (path < 0) {
     const char* e = getenv("QWEN_GEMV_PATH");
-    path = (e && std::strcmp(e, "mma") == 0) ? 1 : 0;
+    path = (e && std::strcmp(e, "mma") == 0) ? 1 : (e && std::strcmp(e, "tc128") == 0) ? 2 : 0;
   }
   return path;
+}
+
+// Weight bytes from which an unpaired launch takes the N = 256 kernel
+// (QWEN_TCW_MIN_MB overrides; default 48 MB).
+static inline long long tcw_min_bytes() {
+  static long long v = -1;
+  if (v < 0) {
+    const char* e = getenv("QWEN_TCW_MIN_MB");
+    v = (e ? atoll(e) : 48ll) << 20;
+  }
+  return v;
 }
 
 // ---------------------------------------------------------------------------
@@ -261,6 +275,100 @@ static cudaError_t gemv_tc_run(GemvArgs a, bool f32_scales, cudaStream_t st, boo
                     : launch_tc_inst<bf16, false>(a, m, grid, L.total, st, pdl);
 }
 
+template <typename ST, bool PAIR>
+static cudaError_t launch_tcw_inst(const GemvArgs& a, const GemvMaps& m, int grid, int smem, cudaStream_t st,
+                                   bool pdl) {
+  auto kern = gemv_tcw_kernel<ST, PAIR>;
+  static bool attr_done[64] = {};
+  const int d = current_device();
+  if (!attr_done[d]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    attr_done[d] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(TW_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a, m);
+}
+
+// Plans and launches the N = 256 tensor-core path (gemv_tcw.cuh); same
+// eligibility as gemv_tc_run.  Units are 256 rows of one matrix or 128 rows
+// of a gate/up pair; one CTA per SM with the deepest ring that fits.
+static cudaError_t gemv_tcw_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool pdl) {
+  const int K = a.K;
+  if (K % 128 != 0 || K < 256) return cudaErrorNotSupported;
+  const int nkb = K / 128;
+  if (!aligned16(a.x) || (a.x2 && !aligned16(a.x2)) || (a.h2_out && !aligned16(a.h2_out)) ||
+      (a.norm_w && !aligned16(a.norm_w)) || (reinterpret_cast<uintptr_t>(a.xn_out) & 7u) != 0)
+    return cudaErrorNotSupported;
+  int npair = 0;
+  for (int s = 0; s < a.nseg; ++s) {
+    const GemvSeg& sg = a.seg[s];
+    if (sg.kblk != nkb || !aligned16(sg.w)) return cudaErrorNotSupported;
+    if (sg.epi == EPI_SILU_PAIR) {
+      if (!aligned16(sg.w2)) return cudaErrorNotSupported;
+      ++npair;
+    }
+  }
+  if (npair != 0 && npair != a.nseg) return cudaErrorNotSupported;
+  const bool pair = npair != 0;
+  const int urows = pair ? 128 : TW_N;
+  GemvMaps m;
+  std::memset(&m, 0, sizeof(m));
+  int nunits = 0;
+  for (int s = 0; s < a.nseg; ++s) {
+    GemvSeg& sg = a.seg[s];
+    sg.unit0 = nunits;
+    nunits += (sg.n + urows - 1) / urows;
+    if (sg.n > 0) {
+      if (!weight_tmap(&m.map[s][0], sg.w, sg.n, K)) return cudaErrorNotSupported;
+      if (pair && !weight_tmap(&m.map[s][1], sg.w2, sg.n, K)) return cudaErrorNotSupported;
+    }
+  }
+  a.nunits = nunits;
+  // K split C: at most 32 K-blocks per item (one scale per lane), else the C
+  // that minimises the busiest CTA's work in 32 KB stages, counting about
+  // one stage of fixed cost per item and the cost of the partial-sum
+  // reduction.  The grid is a multiple of C.
+  const int sms = sm_count();
+  int best_c = 0;
+  double best_cost = 0;
+  const int cmin = (nkb + 31) / 32;
+  for (int c = cmin; c <= nkb && c <= 64 && c <= sms; ++c) {
+    const long long items = (long long)nunits * c;
+    if (c > 1 && (items * TW_N > TC_PART_FLOATS || nunits > TC_MAX_CNT)) break;
+    const long long slots = (long long)(sms / c) * c;
+    const long long waves = (items + slots - 1) / slots;
+    const double cost = (double)waves * ((nkb + c - 1) / c + 1) + (c > 1 ? 1.0 + c / 8.0 : 0.0);
+    if (best_c == 0 || cost < best_cost) {
+      best_c = c;
+      best_cost = cost;
+    }
+  }
+  if (best_c == 0) return cudaErrorNotSupported;
+  a.nslice = best_c;
+  const long long items = (long long)nunits * best_c;
+  const long long slots = (long long)(sms / best_c) * best_c;
+  const int grid = (int)(items < slots ? items : slots);
+  const int S = tw_stages_for(K, best_c, TC_SMEM_MAX);
+  if (S == 0) return cudaErrorNotSupported;
+  a.stages = S;
+  const TwSmem L = tw_smem_layout(K, best_c, S);
+  if (pair)
+    return f32_scales ? launch_tcw_inst<float, true>(a, m, grid, L.total, st, pdl)
+                      : launch_tcw_inst<bf16, true>(a, m, grid, L.total, st, pdl);
+  return f32_scales ? launch_tcw_inst<float, false>(a, m, grid, L.total, st, pdl)
+                    : launch_tcw_inst<bf16, false>(a, m, grid, L.total, st, pdl);
+}
+
 // Validate, plan and launch.  `f32_scales` selects FP32 scale storage.
 // Returns cudaErrorInvalidValue on bad arguments (nothing launched).
 static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool pdl, bool force_simple = false) {
@@ -284,8 +392,21 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
     rows += sg.n;
   }
   if (rows == 0) return cudaSuccess;
-  if (!force_simple && gemv_path() == 0) {
-    const cudaError_t e = gemv_tc_run(a, f32_scales, st, pdl);
+  if (!force_simple && (gemv_path() == 0 || gemv_path() == 2)) {
+    // The N = 256 kernel needs a whole SM per CTA, so it cannot start beside
+    // the previous launch; it pays off for gate/up pairs and for launches
+    // that stream at least tcw_min_bytes() of weights.
+    bool wide = gemv_path() == 0;
+    if (wide) {
+      long long bytes = 0;
+      bool pair = false;
+      for (int s = 0; s < a.nseg; ++s) {
+        bytes += (long long)a.seg[s].n * a.K * (a.seg[s].epi == EPI_SILU_PAIR ? 2 : 1);
+        pair |= a.seg[s].epi == EPI_SILU_PAIR;
+      }
+      wide = pair || bytes >= tcw_min_bytes();
+    }
+    const cudaError_t e = wide ? gemv_tcw_run(a, f32_scales, st, pdl) : gemv_tc_run(a, f32_scales, st, pdl);
     if (e != cudaErrorNotSupported) return e;
   }
   if (npair != 0 && npair != a.nseg) mma_ok = false;

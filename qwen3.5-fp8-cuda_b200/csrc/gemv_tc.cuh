@@ -74,8 +74,8 @@ __device__ unsigned int g_tc_cnt[TC_MAX_CNT];
 
 // Shared memory plan (offsets from a 1024-byte aligned base): the ring of
 // weight stages, the B operand of this CTA's K slice (at most ceil(nkb / C)
-// blocks), BF16 staging of x for the prologue, the RMSNorm weights of the
-// slice, 2^-e per slice block, the mbarriers and a small misc area.
+// blocks), BF16 staging of the slice of x, the RMSNorm weights of the slice,
+// 2^-e per slice block, the mbarriers and a small misc area.
 struct TcSmem {
   int ring_off, xb_off, stg_off, nw_off, xinv_off, bar_off, misc_off, total, stage_bytes;
 };
@@ -87,7 +87,7 @@ __host__ __device__ inline TcSmem tc_smem_layout(int K, int P, int C, int stages
   L.ring_off = 0;
   L.xb_off = stages * L.stage_bytes;
   L.stg_off = L.xb_off + nxb * TC_XBLK;
-  L.nw_off = L.stg_off + nkb * 256;
+  L.nw_off = L.stg_off + nxb * 256;
   L.xinv_off = L.nw_off + nxb * 512;
   L.bar_off = L.xinv_off + align_up(4 * nxb, 16);
   L.misc_off = L.bar_off + 1024;
@@ -160,12 +160,24 @@ __device__ __forceinline__ void tc_ld2(uint32_t taddr, uint32_t& v0, uint32_t& v
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
+// Rows 2.. of every slice block of the x operand (XBLK bytes per K-block)
+// are zero; rows 0 and 1 are written by tc_x_prepare.  Static: runs before
+// griddepcontrol.wait.
+template <int XBLK = TC_XBLK>
+__device__ __forceinline__ void tc_x_zero(int nxb, uint8_t* xbg) {
+  for (int o = (threadIdx.x - 64) * 16; o < nxb * XBLK; o += 192 * 16)
+    if ((o & (XBLK - 1)) >= 256) *reinterpret_cast<uint4*>(xbg + o) = make_uint4(0, 0, 0, 0);
+}
+
 // x -> B operand of K-blocks [kb0, kb0 + nxb) (warps 2..7, 192 threads;
 // named barrier 1).  Pass 1 reads x once (h = x + x2 for ADD_RMSNORM), sums
-// squares over the whole of K and stages the blocks it needs in shared
+// squares over the whole of K and stages the slice's blocks in shared
 // memory; pass 2 normalises, splits into E4M3 hi / lo and writes the
-// swizzled B operand.  CTA 0 also writes h2_out and, over every block, xn_out.
+// swizzled B operand.  CTA 0 also writes h2_out and, over every block, xn_out
+// (re-reading the blocks outside its slice).  XBLK: bytes per K-block of the
+// operand (rows 0 and 1 of a 128-byte-swizzled row group).
 // ---------------------------------------------------------------------------
+template <int XBLK = TC_XBLK>
 __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb, uint8_t* xbg, uint8_t* stg,
                                              const float* nws, float* xinv, float* red) {
   const int K = a.K, nkb = K >> 7;
@@ -174,10 +186,7 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
   const bf16* xin = a.x;
   if (a.x_row) xin += (size_t)(*a.x_row) * K;
   const bool all = blockIdx.x == 0 && a.xn_out != nullptr && a.pro != PRO_NONE;
-  const int sb0 = all ? 0 : kb0, sb1 = all ? nkb : kb0 + nxb;  // staged blocks
-  // zero rows 2..15 of every slice block (rows 0 and 1 are written in pass 2)
-  for (int o = t * 16; o < nxb * TC_XBLK; o += NT * 16)
-    if ((o & (TC_XBLK - 1)) >= 256) *reinterpret_cast<uint4*>(xbg + o) = make_uint4(0, 0, 0, 0);
+  const int sb0 = all ? 0 : kb0, sb1 = all ? nkb : kb0 + nxb;  // blocks of pass 2
   // pass 1: up to MAXC chunks of 8 elements per thread are loaded before any
   // is used, so the loads overlap
   float ss = 0.f;
@@ -214,7 +223,7 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
         ss = fmaf(f.y, f.y, ss);
       }
       const int b = i >> 4;  // 16 chunks of 8 elements per 128-block
-      if (b >= sb0 && b < sb1) reinterpret_cast<uint4*>(stg)[i - sb0 * 16] = v[j];
+      if (b >= kb0 && b < kb0 + nxb) reinterpret_cast<uint4*>(stg)[i - kb0 * 16] = v[j];
     }
   }
   ss = warp_sum(ss);
@@ -230,10 +239,23 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
   // pass 2: one warp per 128-wide block, 4 elements per lane
   for (int b = sb0 + w; b < sb1; b += NW) {
     const int k0 = b * 128 + lane * 4;
-    const uint2 raw = reinterpret_cast<const uint2*>(stg)[(b - sb0) * 32 + lane];
-    const float2 v01 = bf2x_to_f2(raw.x), v23 = bf2x_to_f2(raw.y);
-    float v[4] = {v01.x, v01.y, v23.x, v23.y};
     const bool in_slice = b >= kb0 && b < kb0 + nxb;
+    float v[4];
+    if (in_slice) {
+      const uint2 raw = reinterpret_cast<const uint2*>(stg)[(b - kb0) * 32 + lane];
+      const float2 v01 = bf2x_to_f2(raw.x), v23 = bf2x_to_f2(raw.y);
+      v[0] = v01.x; v[1] = v01.y; v[2] = v23.x; v[3] = v23.y;
+    } else {  // CTA 0 writing xn_out: the same h as pass 1, from global memory
+      const uint2 raw = *reinterpret_cast<const uint2*>(xin + k0);
+      const float2 v01 = bf2x_to_f2(raw.x), v23 = bf2x_to_f2(raw.y);
+      v[0] = v01.x; v[1] = v01.y; v[2] = v23.x; v[3] = v23.y;
+      if (a.pro == PRO_ADD_RMSNORM) {
+        const uint2 r2 = *reinterpret_cast<const uint2*>(a.x2 + k0);
+        const float2 g01 = bf2x_to_f2(r2.x), g23 = bf2x_to_f2(r2.y);
+        v[0] = bfround(v[0] + g01.x); v[1] = bfround(v[1] + g01.y);
+        v[2] = bfround(v[2] + g23.x); v[3] = bfround(v[3] + g23.y);
+      }
+    }
     if (a.pro != PRO_NONE) {
       const float4 wn = in_slice ? reinterpret_cast<const float4*>(nws)[(b - kb0) * 32 + lane]
                                  : __ldg(reinterpret_cast<const float4*>(a.norm_w + k0));
@@ -269,7 +291,7 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
     const uint32_t l23 = f32x2_to_e4m3x2((xs[2] - g23.x) * 32.f, (xs[3] - g23.y) * 32.f);
     // 128-byte swizzle: 16-byte chunk c of row n sits at chunk c ^ n
     const int c = lane >> 2, within = (lane & 3) * 4;
-    uint8_t* blk = xbg + (b - kb0) * TC_XBLK;
+    uint8_t* blk = xbg + (b - kb0) * XBLK;
     *reinterpret_cast<uint32_t*>(blk + (c << 4) + within) = h01 | (h23 << 16);
     *reinterpret_cast<uint32_t*>(blk + 128 + ((c ^ 1) << 4) + within) = l01 | (l23 << 16);
     if (lane == 0) xinv[b - kb0] = exp2i(-e);
@@ -427,6 +449,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ---------------- x preparation (warps 2..7), then epilogue (warps 4..7) ----------------
     if (warp == 2) l2_prefetch_share(a.pf, lane);  // next launch's weights (static data)
+    tc_x_zero(cnxb, gbase + L.xb_off);
     pdl_wait();
     tc_x_prepare(a, ckb0, cnxb, gbase + L.xb_off, gbase + L.stg_off,
                  reinterpret_cast<const float*>(gbase + L.nw_off), xinv, red);
@@ -455,25 +478,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         float acc[P];
 #pragma unroll
         for (int p = 0; p < P; ++p) acc[p] = 0.f;
-        for (int kb = t.kb0; kb < t.kb1; ++kb, ++it) {
-          const int ts = it % TS;
-          if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(tfull_bar(ts), (it / TS) & 1));
+        // K-blocks in groups of G = TS / 2: one wait on the group's last
+        // block (a commit covers every earlier MMA of the issuing thread), G
+        // TMEM loads in flight, one wait::ld.  The MMA issuer meanwhile fills
+        // the other half of the slots.
+        constexpr int G = TS / 2;
+        for (int g0 = t.kb0; g0 < t.kb1; g0 += G, it += G) {
+          const int n = t.kb1 - g0 < G ? t.kb1 - g0 : G;
+          const int itl = it + n - 1;
+          if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(tfull_bar(itl % TS), (itl / TS) & 1));
           if (!ok) continue;
           tc_fence_after();
-          uint32_t v[2 * P];
+          uint32_t v[G][2 * P];
 #pragma unroll
-          for (int p = 0; p < P; ++p) tc_ld2(tl + ts * (16 * P) + p * 16, v[2 * p], v[2 * p + 1]);
+          for (int j = 0; j < G; ++j)
+            if (j < n) {
+              const int ts = (it + j) % TS;
+#pragma unroll
+              for (int p = 0; p < P; ++p) tc_ld2(tl + ts * (16 * P) + p * 16, v[j][2 * p], v[j][2 * p + 1]);
+            }
           tc_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(tempty_bar(ts));
-          const float f = xinv[kb - ckb0];
+          if (lane < n) mbar_arrive(tempty_bar((it + lane) % TS));
 #pragma unroll
-          for (int p = 0; p < P; ++p) {
-            const float sf = __shfl_sync(0xffffffffu, scl[p], kb - t.kb0) * f;
-            acc[p] = fmaf(__uint_as_float(v[2 * p]) + __uint_as_float(v[2 * p + 1]) * 0.03125f, sf, acc[p]);
-          }
+          for (int j = 0; j < G; ++j)
+            if (j < n) {
+              const int kb = g0 + j;
+              const float f = xinv[kb - ckb0];
+#pragma unroll
+              for (int p = 0; p < P; ++p) {
+                const float sf = __shfl_sync(0xffffffffu, scl[p], kb - t.kb0) * f;
+                acc[p] = fmaf(__uint_as_float(v[j][2 * p]) + __uint_as_float(v[j][2 * p + 1]) * 0.03125f, sf, acc[p]);
+              }
+            }
         }
+        it += t.kb1 - t.kb0 - ((t.kb1 - t.kb0 + G - 1) / G) * G;  // undo the last group's overshoot
         const int row = t.row0 + r;
         if (C == 1) {
           if (row < sg.n) am_best = gemv_epilogue(sg, row, acc[0], PAIR ? acc[P - 1] : 0.f, am_best);
@@ -488,13 +528,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           named_bar(2, 128);
           if (*last_flag) {
             __threadfence();
+            // up to 8 slices' loads in flight at once, added in slice order
             float tot[P];
 #pragma unroll
             for (int p = 0; p < P; ++p) tot[p] = 0.f;
-            for (int c = 0; c < C; ++c) {
-              const float* pp = g_tc_part + (size_t)(t.unit * C + c) * P * TC_ROWS;
+            for (int c0 = 0; c0 < C; c0 += 8) {
+              float v[8][P];
 #pragma unroll
-              for (int p = 0; p < P; ++p) tot[p] += __ldcg(pp + p * TC_ROWS + r);
+              for (int j = 0; j < 8; ++j) {
+                const float* pp = g_tc_part + (size_t)(t.unit * C + c0 + j) * P * TC_ROWS;
+#pragma unroll
+                for (int p = 0; p < P; ++p) v[j][p] = c0 + j < C ? __ldcg(pp + p * TC_ROWS + r) : 0.f;
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int p = 0; p < P; ++p)
+                  if (c0 + j < C) tot[p] += v[j][p];
             }
             if (row < sg.n) am_best = gemv_epilogue(sg, row, tot[0], PAIR ? tot[P - 1] : 0.f, am_best);
             if (threadIdx.x == 128) g_tc_cnt[t.unit] = 0u;

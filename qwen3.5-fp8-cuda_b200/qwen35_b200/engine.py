@@ -47,10 +47,16 @@ def rope_tables(max_pos: int, rotary_dim: int, theta: float):
 
 
 class Qwen35DecodeEngine:
-    """Greedy batch-1 decoder over device-resident weights (see ``weights.py``)."""
+    """Greedy batch-1 decoder over device-resident weights (see ``weights.py``).
+
+    ``prefetch=True`` makes every launch pull its successor's weights into L2
+    (``cp.async.bulk.prefetch``) while it runs.  It is off by default: on B200
+    the prefetches compete with the running launch's own stream and the step
+    measured about 8% slower with them.
+    """
 
     def __init__(self, cfg, weights, max_seq: int = 4096, device="cuda", keep_logits: bool = False,
-                 attn_chunk: int | None = None, prefetch: bool = True):
+                 attn_chunk: int | None = None, prefetch: bool = False):
         self.cfg = cfg
         self.prefetch = prefetch
         self.w = weights
@@ -156,7 +162,7 @@ class Qwen35DecodeEngine:
                     _p(self.cos), _p(self.sin), _p(self.k_cache[i]), _p(self.v_cache[i]), _p(self.pos),
                     self.max_seq, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim, cfg.rotary_dim, eps,
                     self.attn_chunk, self.attn_nsplit, _p(self.attn_ws), _p(self.attn_cnt), _p(self.attn_out), st),
-                    "attn_decode"), self._regions(self.k_cache[i], self.v_cache[i])))
+                    "attn_decode"), []))  # a decode step reads pos + 1 cache rows, not the whole cache
                 plan.append((lambda st, wo=wo, so=so: chk(lib.qwen_linear_resid(
                     _p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
                     _p(self.hidden), _p(self.h2), st), "o_proj"), self._regions(wo)))
@@ -196,7 +202,7 @@ class Qwen35DecodeEngine:
         return plan
 
     def _launch_step(self, stream):
-        """Issue one decode step; every launch prefetches its successor's regions."""
+        """Issue one decode step (with prefetch on, every launch prefetches its successor's regions)."""
         plan = self._plan_step()
         st = P(stream)
         n = len(plan)

@@ -13,6 +13,13 @@ own gemv_v4_kernel, whose outputs are exactly the BF16 roundings of the FP32
 oracle on the committed fixture, measures 2.3e-3 in the max-norm form.  The
 max-norm check therefore uses the BF16 unit roundoff (plus accumulation slack).
 
+The normwise bound is applied from 128 outputs up: on fewer outputs it is
+dominated by where individual values fall relative to BF16 rounding
+boundaries.  GEMV outputs are additionally checked element by element with
+assert_rounded(): every output must be a correct BF16 rounding of the FP32
+oracle value, up to an FP32-accumulation slack of 1e-5 of the largest
+|y_ref| (summation order differs between the kernels and the oracle).
+
 Integer / index results (greedy token ids) must be equal.
 """
 
@@ -40,10 +47,23 @@ def cosine(y, ref) -> float:
 
 def assert_close(y, ref, max_rel_err=MAX_REL, min_cos=MIN_COS, rel_l2_err=REL_L2, what=""):
     r, l2, c = max_rel(y, ref), rel_l2(y, ref), cosine(y, ref)
-    assert r <= max_rel_err and l2 <= rel_l2_err and c >= min_cos, (
+    l2_ok = l2 <= rel_l2_err or y.numel() < 128
+    assert r <= max_rel_err and l2_ok and c >= min_cos, (
         f"{what}: max_rel={r:.3e} (<= {max_rel_err}) rel_l2={l2:.3e} (<= {rel_l2_err}) "
         f"cos={c:.8f} (>= {min_cos})")
     return r, l2, c
+
+
+def assert_rounded(y, ref, slack=1e-5, what=""):
+    """Every BF16 output y_i lies within half a BF16 ulp of the FP32 oracle
+    value ref_i, plus slack * max|ref|."""
+    y, ref = y.double().reshape(-1).cpu(), ref.double().reshape(-1).cpu()
+    ulp = torch.pow(2.0, torch.floor(torch.log2(ref.abs().clamp_min(1e-30))) - 7)
+    bound = 0.5 * ulp + slack * float(ref.abs().max())
+    bad = (y - ref).abs() > bound
+    assert not bool(bad.any()), (
+        f"{what}: {int(bad.sum())} of {y.numel()} outputs are not BF16 roundings of the oracle; "
+        f"worst excess {float(((y - ref).abs() - bound).max()):.3e}")
 
 
 def bf16_ulp_diff(y, ref_bf16):

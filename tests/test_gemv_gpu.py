@@ -14,7 +14,7 @@ import torch
 
 from conftest import REF_LIB
 from oracle import ops, synth
-from parity import assert_close, bf16_ulp_diff
+from parity import assert_close, assert_rounded, bf16_ulp_diff
 
 pytestmark = pytest.mark.gpu
 
@@ -55,6 +55,7 @@ def test_config0_gemv(lib):
     y = run_gemv(lib, x, w, s, ops.scale_mode(9216, s))
     ref = oracle_f32(x, w, s, 20)
     assert_close(y, ref, what="config0")
+    assert_rounded(y, ref, what="config0")
     # against the oracle's own BF16 output: almost all elements identical
     assert float((bf16_ulp_diff(y, ref.to(BF16)) > 0).float().mean()) < 0.01
 
@@ -67,7 +68,9 @@ def test_config1_layer_shapes(lib, name, n, k):
     s = s32.to(BF16)
     kblk = ops.scale_mode(n, s)
     y = run_gemv(lib, x, w, s, kblk)
-    assert_close(y, oracle_f32(x, w, s, kblk), what=name)
+    ref = oracle_f32(x, w, s, kblk)
+    assert_close(y, ref, what=name)
+    assert_rounded(y, ref, what=name)
 
 
 @pytest.mark.parametrize("mode", ["per_row", "per_row_block"])
@@ -101,7 +104,9 @@ def test_ragged_shapes(lib, n, k):
     s = s32.to(BF16)
     kblk = ops.scale_mode(n, s)
     y = run_gemv(lib, x, w, s, kblk)
-    assert_close(y, oracle_f32(x, w, s, kblk), what=f"{n}x{k}")
+    ref = oracle_f32(x, w, s, kblk)
+    assert_close(y, ref, what=f"{n}x{k}")
+    assert_rounded(y, ref, what=f"{n}x{k}")
 
 
 @pytest.mark.parametrize("n,k", [(9216, 2560), (2560, 9216), (2560, 4096)])
