@@ -301,7 +301,7 @@ static cudaError_t launch_tcw_inst(const GemvArgs& a, const GemvMaps& m, int gri
 
 // Plans and launches the N = 256 tensor-core path (gemv_tcw.cuh); same
 // eligibility as gemv_tc_run.  Units are 256 rows of one matrix or 128 rows
-// of a gate/up pair; one CTA per SM with the deepest ring that fits.
+// of a gate/up pair.
 static cudaError_t gemv_tcw_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool pdl) {
   const int K = a.K;
   if (K % 128 != 0 || K < 256) return cudaErrorNotSupported;
@@ -358,6 +358,9 @@ static cudaError_t gemv_tcw_run(GemvArgs a, bool f32_scales, cudaStream_t st, bo
   const long long items = (long long)nunits * best_c;
   const long long slots = (long long)(sms / best_c) * best_c;
   const int grid = (int)(items < slots ? items : slots);
+  // One CTA per SM: each CTA holds all 512 TMEM columns, so two CTAs of one
+  // grid on an SM would run one after the other (the second waits in
+  // tcgen05.alloc).  The ring takes the whole shared memory instead.
   const int S = tw_stages_for(K, best_c, TC_SMEM_MAX);
   if (S == 0) return cudaErrorNotSupported;
   a.stages = S;

@@ -23,7 +23,7 @@
 //   D = 256 FP32 columns per K-block; two accumulators (512 TMEM columns)
 //       alternate between K-blocks.
 //
-// Roles (256 threads, one CTA per SM): warp 0 lane 0 streams the weight
+// Roles (256 threads, up to 128 registers each): warp 0 lane 0 streams the weight
 // tiles (32 KB stages, filled before griddepcontrol.wait); warp 1 lane 0
 // issues four MMAs per K-block and commits the stage and the accumulator;
 // warps 2-7 prepare x; warps 4-7 (lane quarter q) read columns 64q..64q+63
@@ -115,8 +115,10 @@ __device__ __forceinline__ TcItem tw_item(const GemvArgs& a, int i, int nkb, int
   return t;
 }
 
+// At most 128 registers per thread.  The host sizes the ring so that one CTA
+// fills an SM's shared memory: a CTA holds all 512 TMEM columns.
 template <typename ST, bool PAIR>
-__global__ void __launch_bounds__(TW_THREADS, 1)
+__global__ void __launch_bounds__(TW_THREADS, 2)
     gemv_tcw_kernel(const __grid_constant__ GemvArgs a, const __grid_constant__ GemvMaps m) {
   constexpr int UROWS = PAIR ? 128 : 256;  // output rows per unit
   extern __shared__ uint8_t smem_raw[];
@@ -285,20 +287,20 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
           const float sf = __shfl_sync(0xffffffffu, scl, kb - t.kb0);
           if (!ok) continue;
           tc_fence_after();
-          uint32_t v0[32], v1[32];
-          tw_ld32(tl + (uint32_t)(b * 256), v0);
-          tw_ld32(tl + (uint32_t)(b * 256 + 32), v1);
-          tc_wait_ld();
+          // lane 0 holds the hi sums, lane 1 the lo sums (weight 1/32); the
+          // two 32-column halves one after the other keep registers low
+          const float f = xinv[kb - ckb0] * sf * (lane == 1 ? 0.03125f : 1.0f);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t v[32];
+            tw_ld32(tl + (uint32_t)(b * 256 + 32 * h), v);
+            tc_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[32 * h + j] = fmaf(__uint_as_float(v[j]), f, acc[32 * h + j]);
+          }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar(b));
-          // lane 0 holds the hi sums, lane 1 the lo sums (weight 1/32)
-          const float f = xinv[kb - ckb0] * sf * (lane == 1 ? 0.03125f : 1.0f);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            acc[j] = fmaf(__uint_as_float(v0[j]), f, acc[j]);
-            acc[32 + j] = fmaf(__uint_as_float(v1[j]), f, acc[32 + j]);
-          }
         }
         // gather: red[c] = hi sum, red[256 + c] = lo sum of column c
         if (lane < 2) {
