@@ -326,6 +326,8 @@ def config_block(args):
                         "decode (E4M3 128x128 block-scaled linear weights incl. LM head)",
             "model": "Qwen3.5-4B (random init)", "global_batch": 1, "prompt_len": PROMPT_LEN,
             "decode_steps": args.steps, "parallelism": f"tp{args.gpus}" if args.gpus > 1 else "single",
+            **({"tp_exchange": "NVLink peer stores of FP32 partials + flags (CUDA IPC), no library collective"}
+               if args.gpus > 1 else {}),
             "l2": "no flush: each step streams ~4.3 GB of weights (> 126 MB L2)"}
 
 
@@ -480,6 +482,7 @@ def run_ours(args):
             line["cpu_baseline"] = {"value": None, "error": repr(exc)[:200]}
     eng.graph = None
     if world > 1:
+        eng.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

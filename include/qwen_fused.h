@@ -152,6 +152,31 @@ int qwen_linear_partial(const void* x, const void* w, const void* s, int N, int 
 int qwen_resid_add_f32(const void* res, const float* v, void* y, int n, cudaStream_t stream);
 /* token = the greedy token id encoded in an all-reduced packed argmax key. */
 int qwen_token_from_key(const long long* key, long long* token, cudaStream_t stream);
+/* Tensor parallelism without a library collective: the partial sums and the
+ * argmax keys are exchanged through a per-rank region mapped into every rank
+ * with CUDA IPC (flags, key slots, counters, 2 x world x n FP32 buffers).
+ * qwen_p2p_create allocates and zeroes this rank's region and writes its
+ * 64-byte IPC handle; qwen_p2p_open maps a peer's; qwen_p2p_table builds the
+ * device table from all regions (bases[rank] = own) for n-element sums. */
+int qwen_p2p_create(int world, int n, void** base_out, void* ipc_handle_out);
+int qwen_p2p_open(const void* ipc_handle, void** peer_base_out);
+int qwen_p2p_close(void* peer_base);
+int qwen_p2p_destroy(void* base);
+int qwen_p2p_table(void* const* bases, int world, int rank, int n, void** table_out);
+int qwen_p2p_table_free(void* table);
+/* The next RMSNorm-prologue launch on this host thread (qwen_attn_in_proj,
+ * qwen_gdn_in_proj, qwen_mlp_gate_up, launch_lm_head_argmax) builds its input
+ * as bf16(res + bf16(sum of the ranks' n-element partials)) after waiting for
+ * every rank's partial (bounded), writes it to the buffer passed as its x,
+ * and normalises it; the launch then advances the exchange round. */
+int qwen_set_p2p_input(const void* table, const void* res, int n);
+/* This rank's partial GEMV, stored into slot [rank] of every rank's buffer. */
+int qwen_linear_partial_p2p(const void* x, const void* w, const void* s, int N, int K, int K_blk, const void* table,
+                            cudaStream_t stream);
+/* y = bf16(res + bf16(sum of the ranks' partials)) once all have arrived (bounded wait). */
+int qwen_resid_add_p2p(const void* table, const void* res, void* y, int n, cudaStream_t stream);
+/* token = greedy token over every rank's packed argmax key (bounded wait). */
+int qwen_token_p2p(const void* table, const long long* key, long long* token, cudaStream_t stream);
 /* silu_out = bf16(silu(g)*u), g/u = GEMVs of RMSNorm(h2) (398-479, 1173-1190). */
 int qwen_mlp_gate_up(const void* h2, const float* norm_w, float eps, const void* w_g, const void* s_g,
                      const void* w_u, const void* s_u, int N, int K, int K_blk, void* silu_out, cudaStream_t stream);

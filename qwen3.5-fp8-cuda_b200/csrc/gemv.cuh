@@ -35,6 +35,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "p2p.cuh"
 
 namespace qwen {
 
@@ -59,12 +60,14 @@ enum GemvEpi : int {
   EPI_GATE_G = 5,     // y(f32)[r] = -exp(A_log[r]) * softplus(bf16(v) + dt_bias[r])
   EPI_GATE_BETA = 6,  // y[r] = bf16(sigmoid(bf16(v)))
   EPI_F32 = 7,        // y(f32)[r] = v (partial sums of a K-sliced tensor-parallel GEMV)
+  EPI_F32_P2P = 8,    // v into slot [rank] of every rank's exchange buffer (aux0 = P2PTable*)
 };
 
 enum GemvPro : int {
   PRO_NONE = 0,         // x as given
   PRO_RMSNORM = 1,      // x <- bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))
   PRO_ADD_RMSNORM = 2,  // h2 <- bf16(x + x2) (stored by CTA 0); x <- rmsnorm(h2)
+  PRO_P2P_RMSNORM = 3,  // h2 <- bf16(x + bf16(sum of the ranks' partials, p2p)) (stored by CTA 0); x <- rmsnorm(h2)
 };
 
 struct GemvSeg {
@@ -105,6 +108,7 @@ struct GemvArgs {
   long long* am_token_out;         // optional: final token id
   int* pos_inc;                    // optional: ++*pos_inc by the argmax finaliser
   L2Prefetch pf;                   // weights of the next launch, pulled into L2 while this one runs
+  const P2PTable* p2p;             // PRO_P2P_RMSNORM: the tensor-parallel exchange of this round
   GemvSeg seg[GEMV_MAX_SEG];
 };
 
@@ -207,6 +211,9 @@ __device__ __noinline__ unsigned long long gemv_epilogue(const GemvSeg& sg, int 
     } break;
     case EPI_F32:
       reinterpret_cast<float*>(sg.y)[r] = v;
+      break;
+    case EPI_F32_P2P:
+      p2p_store_row(static_cast<const P2PTable*>(sg.aux0), r, v);
       break;
     default:
       break;

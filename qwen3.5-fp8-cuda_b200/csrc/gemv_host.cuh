@@ -385,7 +385,8 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
   for (int s = 0; s < a.nseg; ++s) {
     GemvSeg& sg = a.seg[s];
     if (sg.n < 0 || !sg.w || !sg.s) return cudaErrorInvalidValue;
-    if (sg.epi != EPI_ARGMAX && sg.n > 0 && !sg.y) return cudaErrorInvalidValue;
+    if (sg.epi != EPI_ARGMAX && sg.epi != EPI_F32_P2P && sg.n > 0 && !sg.y) return cudaErrorInvalidValue;
+    if (sg.epi == EPI_F32_P2P && !sg.aux0) return cudaErrorInvalidValue;
     if (sg.epi == EPI_SILU_PAIR && (!sg.w2 || !sg.s2)) return cudaErrorInvalidValue;
     if (sg.epi == EPI_CONV && (sg.cw < 1 || sg.cw > 8 || !sg.aux0 || !sg.aux2)) return cudaErrorInvalidValue;
     if (sg.epi == EPI_ARGMAX && !a.am_ws) return cudaErrorInvalidValue;
@@ -412,6 +413,7 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
     const cudaError_t e = wide ? gemv_tcw_run(a, f32_scales, st, pdl) : gemv_tc_run(a, f32_scales, st, pdl);
     if (e != cudaErrorNotSupported) return e;
   }
+  if (a.pro == PRO_P2P_RMSNORM) return cudaErrorNotSupported;  // tcgen05 kernels only
   if (npair != 0 && npair != a.nseg) mma_ok = false;
   if (mma_ok && (a.K / 128 + GEMV_WARPS - 1) / GEMV_WARPS > 32) mma_ok = false;  // K > 32768
   if (mma_ok) {

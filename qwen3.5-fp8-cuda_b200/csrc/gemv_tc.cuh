@@ -187,11 +187,74 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
   if (a.x_row) xin += (size_t)(*a.x_row) * K;
   const bool all = blockIdx.x == 0 && a.xn_out != nullptr && a.pro != PRO_NONE;
   const int sb0 = all ? 0 : kb0, sb1 = all ? nkb : kb0 + nxb;  // blocks of pass 2
+  // Tensor-parallel input: publish this rank's partial of the round (CTA 0),
+  // wait for every rank's (bounded), then read the slots below.
+  const float* pbuf = nullptr;
+  int pworld = 0, pn = 0;
+  if (a.pro == PRO_P2P_RMSNORM) {
+    const P2PTable& pt = *a.p2p;
+    const unsigned s = *reinterpret_cast<const volatile unsigned*>(pt.seq);
+    if (t == 0) {
+      if (blockIdx.x == 0) p2p_publish(pt, s & 1u, s + 1u);
+      if (!p2p_wait_all(pt, s & 1u, s + 1u)) qwen_err_set(ERR_P2P_TIMEOUT);
+    }
+    pbuf = pt.buf[pt.rank][s & 1u];
+    pworld = pt.world;
+    pn = pt.n;
+    named_bar(1, NT);
+  }
   // pass 1: up to MAXC chunks of 8 elements per thread are loaded before any
   // is used, so the loads overlap
   float ss = 0.f;
   const int nch = K >> 3;
-  for (int base = t; base < nch; base += NT * MAXC) {
+  // Tensor-parallel input: h = bf16(res + bf16(sum of the ranks' partials in
+  // rank order)), two chunks per thread in flight, the ranks' loads of both
+  // chunks issued before they are added.
+  for (int base = t; a.pro == PRO_P2P_RMSNORM && base < nch; base += NT * 2) {
+    uint4 v[2];
+    float sum[2][8];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = base + j * NT;
+      if (i < nch) v[j] = __ldg(reinterpret_cast<const uint4*>(xin) + i);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum[j][e] = 0.f;
+    }
+    for (int src = 0; src < pworld; ++src) {
+      float4 pv[2][2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int i = base + j * NT;
+        const float4* pp = reinterpret_cast<const float4*>(pbuf + (size_t)src * pn + (size_t)(i < nch ? i : 0) * 8);
+        pv[j][0] = __ldcv(pp);
+        pv[j][1] = __ldcv(pp + 1);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        sum[j][0] += pv[j][0].x; sum[j][1] += pv[j][0].y; sum[j][2] += pv[j][0].z; sum[j][3] += pv[j][0].w;
+        sum[j][4] += pv[j][1].x; sum[j][5] += pv[j][1].y; sum[j][6] += pv[j][1].z; sum[j][7] += pv[j][1].w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = base + j * NT;
+      if (i >= nch) continue;
+      uint32_t* vw = reinterpret_cast<uint32_t*>(&v[j]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = bf2x_to_f2(vw[q]);
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f.x + bfround(sum[j][2 * q]), f.y + bfround(sum[j][2 * q + 1]));
+        vw[q] = *reinterpret_cast<const uint32_t*>(&h);
+        const float2 g = bf2x_to_f2(vw[q]);
+        ss = fmaf(g.x, g.x, ss);
+        ss = fmaf(g.y, g.y, ss);
+      }
+      if (blockIdx.x == 0 && a.h2_out) reinterpret_cast<uint4*>(a.h2_out)[i] = v[j];
+      const int b = i >> 4;
+      if (b >= kb0 && b < kb0 + nxb) reinterpret_cast<uint4*>(stg)[i - kb0 * 16] = v[j];
+    }
+  }
+  for (int base = t; a.pro != PRO_P2P_RMSNORM && base < nch; base += NT * MAXC) {
     uint4 v[MAXC], r[MAXC];
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
@@ -559,6 +622,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   if (a.am_ws) argmax_finish(a, am_best, am_misc);
+  if (a.pro == PRO_P2P_RMSNORM && threadIdx.x == 0) p2p_round_done(*a.p2p);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TC_TMEM_COLS) : "memory");

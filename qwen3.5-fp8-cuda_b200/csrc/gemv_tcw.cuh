@@ -365,6 +365,7 @@ __global__ void __launch_bounds__(TW_THREADS, 2)
   tc_fence_before();
   __syncthreads();
   if (a.am_ws) argmax_finish(a, am_best, am_misc);
+  if (a.pro == PRO_P2P_RMSNORM && threadIdx.x == 0) p2p_round_done(*a.p2p);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TW_TMEM_COLS) : "memory");

@@ -32,6 +32,29 @@ inline L2Prefetch take_prefetch() {
   return pf;
 }
 
+// Tensor-parallel input of the next RMSNorm-prologue launch on this host
+// thread (set by qwen_set_p2p_input, consumed and cleared by that launch):
+// the launch builds its x as bf16(res + bf16(sum of the ranks' partials)),
+// writes it to the buffer it was given as x, and normalises it.
+thread_local const void* g_p2p_table = nullptr;
+thread_local const void* g_p2p_res = nullptr;
+thread_local int g_p2p_n = 0;
+
+inline cudaError_t take_p2p_input(GemvArgs& a) {
+  if (!g_p2p_table) return cudaSuccess;
+  const void* t = g_p2p_table;
+  const void* r = g_p2p_res;
+  const int n = g_p2p_n;
+  g_p2p_table = g_p2p_res = nullptr;
+  g_p2p_n = 0;
+  if (a.pro != PRO_RMSNORM || n != a.K || a.xn_out || a.h2_out || a.x_row) return cudaErrorInvalidValue;
+  a.pro = PRO_P2P_RMSNORM;
+  a.p2p = static_cast<const P2PTable*>(t);
+  a.h2_out = const_cast<bf16*>(a.x);
+  a.x = static_cast<const bf16*>(r);
+  return cudaSuccess;
+}
+
 inline int record(cudaError_t e) {
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) g_last_error = (int)e;
@@ -79,6 +102,21 @@ int mlp_tail(const void* h2_src_a, const void* h2_src_b, const float* norm_w, co
 
 }  // namespace
 
+// Tensor-parallel exchange helpers (used by the qwen_p2p_* / *_p2p exports).
+static size_t p2p_region_bytes(int world, int n) { return P2P_DATA_OFF + 2ull * world * n * sizeof(float); }
+static cudaError_t launch_small(const void* kern, int grid, int block, void** args, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = engine_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kern, args);
+}
+
 extern "C" {
 
 // ---------------------------------------------------------------------------
@@ -106,6 +144,17 @@ void qwen_set_pdl(int enable) { g_pdl_enabled = enable; }
 // Weight regions (up to four; null / 0 entries ignored) that the next engine
 // launch issued on this host thread pulls into L2 while it runs -- normally
 // the weights of the launch after it.  Sizes are rounded down to 16 bytes.
+// The next RMSNorm-prologue launch on this host thread takes its input from
+// the tensor-parallel exchange `table` (n-element partial sums) plus the
+// residual `res` (see take_p2p_input).
+int qwen_set_p2p_input(const void* table, const void* res, int n) {
+  if (!table || !res || n <= 0) return record(cudaErrorInvalidValue);
+  g_p2p_table = table;
+  g_p2p_res = res;
+  g_p2p_n = n;
+  return 0;
+}
+
 void qwen_set_prefetch(const void* p0, unsigned long long n0, const void* p1, unsigned long long n1,
                        const void* p2, unsigned long long n2, const void* p3, unsigned long long n3) {
   const void* p[4] = {p0, p1, p2, p3};
@@ -376,6 +425,7 @@ int launch_lm_head_argmax(const void* x, const float* norm_w, float eps, const v
   a.am_token_out = token_out;
   a.pos_inc = pos_inc;
   a.pf = take_prefetch();
+  if (cudaError_t pe = take_p2p_input(a)) return record(pe);
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -418,6 +468,7 @@ int qwen_attn_in_proj(const void* hidden, const float* norm_w, float eps, const 
   a.seg[1] = seg(w_k, s_k, k_out, N_k, K_blk);
   a.seg[2] = seg(w_v, s_v, v_out, N_v, K_blk);
   a.pf = take_prefetch();
+  if (cudaError_t pe = take_p2p_input(a)) return record(pe);
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -445,6 +496,7 @@ int qwen_gdn_in_proj(const void* hidden, const float* norm_w, float eps, int K, 
   a.seg[2].aux1 = dt_bias;
   a.seg[3] = seg(w_b, s_b, beta_out, N_heads, K_blk, EPI_GATE_BETA);
   a.pf = take_prefetch();
+  if (cudaError_t pe = take_p2p_input(a)) return record(pe);
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -527,6 +579,106 @@ int qwen_token_from_key(const long long* key, long long* token, cudaStream_t str
                                    token));
 }
 
+// ---------------------------------------------------------------------------
+// Tensor parallel over NVLink peer memory (p2p.cuh)
+// ---------------------------------------------------------------------------
+// Allocates this rank's exchange region for `world` ranks and n-element
+// partial sums (zeroed) and writes its CUDA IPC handle (64 bytes).
+int qwen_p2p_create(int world, int n, void** base_out, void* ipc_handle_out) {
+  if (world < 1 || world > P2P_MAX_WORLD || n <= 0 || !base_out || !ipc_handle_out)
+    return record(cudaErrorInvalidValue);
+  void* base = nullptr;
+  const size_t bytes = p2p_region_bytes(world, n);
+  cudaError_t e = cudaMalloc(&base, bytes);
+  if (e != cudaSuccess) return record(e);
+  e = cudaMemset(base, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, base);
+  if (e != cudaSuccess) {
+    cudaFree(base);
+    return record(e);
+  }
+  std::memcpy(ipc_handle_out, &h, sizeof(h));
+  *base_out = base;
+  return 0;
+}
+
+// Maps another rank's exchange region (its IPC handle) into this process.
+int qwen_p2p_open(const void* ipc_handle, void** peer_base_out) {
+  if (!ipc_handle || !peer_base_out) return record(cudaErrorInvalidValue);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return record(cudaIpcOpenMemHandle(peer_base_out, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int qwen_p2p_close(void* peer_base) { return record(cudaIpcCloseMemHandle(peer_base)); }
+int qwen_p2p_destroy(void* base) { return record(cudaFree(base)); }
+
+// Builds the device table of a rank: bases[p] = rank p's region as mapped in
+// this process (bases[rank] = its own).  Returns a device pointer.
+int qwen_p2p_table(void* const* bases, int world, int rank, int n, void** table_out) {
+  if (!bases || world < 1 || world > P2P_MAX_WORLD || rank < 0 || rank >= world || n <= 0 || !table_out)
+    return record(cudaErrorInvalidValue);
+  P2PTable t;
+  std::memset(&t, 0, sizeof(t));
+  for (int p = 0; p < world; ++p) {
+    char* b = static_cast<char*>(bases[p]);
+    if (!b) return record(cudaErrorInvalidValue);
+    t.flag[p] = reinterpret_cast<unsigned*>(b);
+    t.key[p] = reinterpret_cast<unsigned long long*>(b + 64);
+    for (int par = 0; par < 2; ++par)
+      t.buf[p][par] = reinterpret_cast<float*>(b + P2P_DATA_OFF) + (size_t)par * world * n;
+  }
+  char* own = static_cast<char*>(bases[rank]);
+  t.seq = reinterpret_cast<unsigned*>(own + 256);
+  t.done = reinterpret_cast<unsigned*>(own + 260);
+  t.world = world;
+  t.rank = rank;
+  t.n = n;
+  void* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, sizeof(t));
+  if (e == cudaSuccess) e = cudaMemcpy(d, &t, sizeof(t), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    if (d) cudaFree(d);
+    return record(e);
+  }
+  *table_out = d;
+  return 0;
+}
+int qwen_p2p_table_free(void* table) { return record(cudaFree(table)); }
+
+// Column-shard GEMV whose FP32 rows go to slot [rank] of every rank's buffer.
+int qwen_linear_partial_p2p(const void* x, const void* w, const void* s, int N, int K, int K_blk, const void* table,
+                            cudaStream_t stream) {
+  if (!table) return record(cudaErrorInvalidValue);
+  GemvArgs a = make_args(x, K);
+  a.nseg = 1;
+  a.seg[0] = seg(w, s, nullptr, N, K_blk, EPI_F32_P2P);
+  a.seg[0].aux0 = table;
+  a.pf = take_prefetch();
+  return record(gemv_run(a, false, stream, engine_pdl()));
+}
+
+// y = bf16(res + bf16(sum over ranks)) once every rank's partial has arrived.
+int qwen_resid_add_p2p(const void* table, const void* res, void* y, int n, cudaStream_t stream) {
+  if (!table || !res || !y || n <= 0) return record(cudaErrorInvalidValue);
+  const P2PTable* t = static_cast<const P2PTable*>(table);
+  const bf16* r = static_cast<const bf16*>(res);
+  bf16* yy = static_cast<bf16*>(y);
+  void* args[] = {&t, &r, &yy};
+  return record(launch_small(reinterpret_cast<const void*>(p2p_resid_kernel), (n + 255) / 256, 256, args, stream));
+}
+
+// token = greedy token over every rank's packed argmax key.
+int qwen_token_p2p(const void* table, const long long* key, long long* token, cudaStream_t stream) {
+  if (!table || !key || !token) return record(cudaErrorInvalidValue);
+  const P2PTable* t = static_cast<const P2PTable*>(table);
+  const unsigned long long* k = reinterpret_cast<const unsigned long long*>(key);
+  void* args[] = {&t, &k, &token};
+  return record(launch_small(reinterpret_cast<const void*>(p2p_token_kernel), 1, 32, args, stream));
+}
+
 // silu_out = bf16(silu(g) * u) with g, u = GEMV(RMSNorm(1+w)(h2)).
 int qwen_mlp_gate_up(const void* h2, const float* norm_w, float eps, const void* w_g, const void* s_g,
                      const void* w_u, const void* s_u, int N, int K, int K_blk, void* silu_out, cudaStream_t stream) {
@@ -539,6 +691,7 @@ int qwen_mlp_gate_up(const void* h2, const float* norm_w, float eps, const void*
   a.seg[0].w2 = static_cast<const uint8_t*>(w_u);
   a.seg[0].s2 = s_u;
   a.pf = take_prefetch();
+  if (cudaError_t pe = take_p2p_input(a)) return record(pe);
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 

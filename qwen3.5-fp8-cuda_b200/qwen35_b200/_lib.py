@@ -68,6 +68,16 @@ NEW_FUSED = {
     "qwen_linear_partial": (I, [P, P, P, I, I, I, P, P]),
     "qwen_resid_add_f32": (I, [P, P, P, I, P]),
     "qwen_token_from_key": (I, [P, P, P]),
+    "qwen_p2p_create": (I, [I, I, P, P]),
+    "qwen_p2p_open": (I, [P, P]),
+    "qwen_p2p_close": (I, [P]),
+    "qwen_p2p_destroy": (I, [P]),
+    "qwen_p2p_table": (I, [P, I, I, I, P]),
+    "qwen_p2p_table_free": (I, [P]),
+    "qwen_linear_partial_p2p": (I, [P, P, P, I, I, I, P, P]),
+    "qwen_resid_add_p2p": (I, [P, P, P, I, P]),
+    "qwen_token_p2p": (I, [P, P, P, P]),
+    "qwen_set_p2p_input": (I, [P, P, I]),
 }
 NEW_FP8 = {
     "qwen_fp8_last_error": (I, []),

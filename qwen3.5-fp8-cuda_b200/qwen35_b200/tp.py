@@ -22,9 +22,20 @@ itself runs on one GPU):
   offset, the packed keys are all-reduced with MAX (one 8-byte value) and
   the token is decoded from the winner: ties still go to the lowest index.
 
-Embedding, norms and the residual stream are replicated.  Collectives go
-through torch.distributed (NCCL) on the engine's stream and are captured
-into the step's CUDA graph with the kernels.
+Embedding, norms and the residual stream are replicated.  The exchanges
+run in one of two ways, both captured into the step's CUDA graph:
+
+* ``collective="p2p"`` (default): no library collective.  The column-split
+  GEMV stores its FP32 partial rows straight into every rank's exchange
+  buffer over NVLink (CUDA IPC mappings, ``qwen_linear_partial_p2p``); the
+  residual kernel publishes a flag to every rank, waits (bounded) for every
+  rank's flag, sums the slots in rank order and adds the residual
+  (``qwen_resid_add_p2p``); the argmax keys go the same way
+  (``qwen_token_p2p``).  See csrc/p2p.cuh for the round protocol.
+* ``collective="nccl"``: ``torch.distributed.all_reduce`` (SUM of the FP32
+  partials, MAX of the packed key) on the engine's stream.
+
+torch.distributed is used for setup in both (the IPC handle exchange).
 """
 
 from __future__ import annotations
@@ -160,20 +171,74 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
     """One rank of the tensor-parallel greedy decoder.
 
     Every rank is driven with the same tokens (the residual stream, position
-    and greedy token are replicated); ``group`` is an initialised NCCL process
-    group of ``world`` ranks, one GPU each.
+    and greedy token are replicated); ``group`` is an initialised process
+    group of ``world`` ranks, one GPU each (NCCL for ``collective="nccl"``).
     """
 
-    def __init__(self, cfg, weights, rank: int, world: int, group=None, **kw):
+    def __init__(self, cfg, weights, rank: int, world: int, group=None, collective: str = "p2p", **kw):
         import torch.distributed as dist
+        if collective not in ("p2p", "nccl"):
+            raise ValueError(f"collective must be 'p2p' or 'nccl', not {collective!r}")
         self.full_cfg = cfg
         self.layout = tp_layout(cfg, rank, world)
         self.dist = dist
         self.group = group
+        self.collective = collective
+        self.rank, self.world = rank, world
         lcfg = local_config(cfg, self.layout)
         lw = shard_weights(cfg, weights, self.layout)
         super().__init__(lcfg, lw, **kw)
         self.partial = torch.zeros(cfg.hidden_size, dtype=torch.float32, device=self.device)
+        self._p2p_base = self._p2p_table = None
+        self._p2p_peers = []
+        if collective == "p2p":
+            self._p2p_setup(cfg.hidden_size)
+        # launches per decoder layer in the plan (the layer-by-layer tests step
+        # through them); with p2p a layer's output stream is written by the
+        # next layer's first launch (or the LM head)
+        self.launches_per_layer = 5 if collective == "p2p" else 9
+
+    def _p2p_setup(self, n: int):
+        """Allocate this rank's exchange region, map every peer's (CUDA IPC)
+        and build the device table."""
+        import ctypes
+        lib, dist = self.lib, self.dist
+        base = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        _lib.check(lib.qwen_p2p_create(self.world, n, ctypes.byref(base), handle), "qwen_p2p_create")
+        self._p2p_base = base
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=self.group)
+        bases = []
+        for r in range(self.world):
+            if r == self.rank:
+                bases.append(base.value)
+                continue
+            pb = ctypes.c_void_p()
+            _lib.check(lib.qwen_p2p_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(pb)),
+                       "qwen_p2p_open")
+            self._p2p_peers.append(pb)
+            bases.append(pb.value)
+        arr = (ctypes.c_void_p * self.world)(*bases)
+        table = ctypes.c_void_p()
+        _lib.check(lib.qwen_p2p_table(arr, self.world, self.rank, n, ctypes.byref(table)), "qwen_p2p_table")
+        self._p2p_table = table
+        dist.barrier(group=self.group)
+
+    def close(self):
+        """Unmap the peers' exchange regions and free this rank's (collective:
+        every rank calls it, after its last step)."""
+        if self._p2p_base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self.dist.barrier(group=self.group)
+        self.graph = None
+        for pb in self._p2p_peers:
+            self.lib.qwen_p2p_close(pb)
+        self.lib.qwen_p2p_table_free(self._p2p_table)
+        self.lib.qwen_p2p_destroy(self._p2p_base)
+        self._p2p_base = self._p2p_table = None
+        self._p2p_peers = []
 
     def _plan_step(self):
         cfg, lib, w, dist = self.cfg, self.lib, self.w, self.dist
@@ -187,8 +252,31 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
         def allreduce_sum(st):
             dist.all_reduce(self.partial, op=dist.ReduceOp.SUM, group=self.group)
 
+        p2p = self.collective == "p2p"
+        table = self._p2p_table
+        # p2p: the launch after a partial GEMV (gate/up, the next in_proj or
+        # the LM head) takes its input from the exchange plus the residual:
+        # no separate reduction launch
+        pending = []
+
+        def add(launch, regions):
+            if pending:
+                res = pending.pop()
+                inner = launch
+
+                def launch(st, inner=inner, res=res):
+                    chk(lib.qwen_set_p2p_input(table, _p(res), H), "p2p_input")
+                    return inner(st)
+            plan.append((launch, regions))
+
         def partial_resid(x, wt, res, out):
             wo, so = wt
+            if p2p:
+                plan.append((lambda st: chk(lib.qwen_linear_partial_p2p(
+                    _p(x), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so), table, st),
+                    "linear_partial_p2p"), self._regions(wo)))
+                pending.append(res)  # the consumer writes bf16(res + sum) to `out`, its x
+                return
             plan.append((lambda st: chk(lib.qwen_linear_partial(
                 _p(x), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
                 _p(self.partial), st), "linear_partial"), self._regions(wo)))
@@ -201,10 +289,10 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
         for i, ly in enumerate(w["layers"]):
             if cfg.layer_types[i] == "full_attention":
                 (wq, sq), (wk, sk), (wv, sv) = ly["q_proj"], ly["k_proj"], ly["v_proj"]
-                plan.append((lambda st, ly=ly, wq=wq, sq=sq, wk=wk, sk=sk, wv=wv, sv=sv: chk(lib.qwen_attn_in_proj(
+                add(lambda st, ly=ly, wq=wq, sq=sq, wk=wk, sk=sk, wv=wv, sv=sv: chk(lib.qwen_attn_in_proj(
                     _p(self.hidden), _p(ly["input_layernorm"]), eps, _p(wq), _p(sq), wq.shape[0], _p(wk), _p(sk),
                     wk.shape[0], _p(wv), _p(sv), wv.shape[0], H, scale_mode(wq.shape[0], sq), _p(self.q_all),
-                    _p(self.k_new), _p(self.v_new), st), "attn_in_proj"), self._regions(wq, wk, wv)))
+                    _p(self.k_new), _p(self.v_new), st), "attn_in_proj"), self._regions(wq, wk, wv))
                 plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_attn_decode(
                     _p(self.q_all), _p(self.k_new), _p(self.v_new), _p(ly["q_norm"]), _p(ly["k_norm"]),
                     _p(self.cos), _p(self.sin), _p(self.k_cache[i]), _p(self.v_cache[i]), _p(self.pos),
@@ -215,29 +303,34 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
             else:
                 (wqkv, sqkv), (wz, sz) = ly["in_proj_qkv"], ly["in_proj_z"]
                 (wa, sa), (wb, sb) = ly["in_proj_a"], ly["in_proj_b"]
-                plan.append((lambda st, ly=ly, i=i, wqkv=wqkv, sqkv=sqkv, wz=wz, sz=sz, wa=wa, sa=sa, wb=wb, sb=sb:
+                add(lambda st, ly=ly, i=i, wqkv=wqkv, sqkv=sqkv, wz=wz, sz=sz, wa=wa, sa=sa, wb=wb, sb=sb:
                              chk(lib.qwen_gdn_in_proj(
                                  _p(self.hidden), _p(ly["input_layernorm"]), eps, H, scale_mode(wqkv.shape[0], sqkv),
                                  _p(wqkv), _p(sqkv), wqkv.shape[0], _p(ly["conv1d_w"]), _p(self.conv_state[i]),
                                  cfg.linear_conv_kernel_dim, _p(self.qkv_conv), _p(wz), _p(sz), wz.shape[0],
                                  _p(self.z), _p(wa), _p(sa), _p(wb), _p(sb), wa.shape[0], _p(ly["A_log"]),
                                  _p(ly["dt_bias"]), _p(self.g), _p(self.beta), st), "gdn_in_proj"),
-                             self._regions(wqkv, wz, wa, wb)))
+                             self._regions(wqkv, wz, wa, wb))
                 plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_gdn_decode(
                     _p(self.qkv_conv), _p(self.g), _p(self.beta), _p(self.state[i]), _p(self.z), _p(ly["norm_w"]),
                     eps, _p(self.attn_out), cfg.linear_num_key_heads, cfg.linear_num_value_heads,
                     cfg.linear_value_head_dim, st), "gdn_decode"), []))
                 partial_resid(self.attn_out, ly["out_proj"], self.hidden, self.h2)
             (wg, sg), (wu, su) = ly["gate_proj"], ly["up_proj"]
-            plan.append((lambda st, ly=ly, wg=wg, sg=sg, wu=wu, su=su: chk(lib.qwen_mlp_gate_up(
+            add(lambda st, ly=ly, wg=wg, sg=sg, wu=wu, su=su: chk(lib.qwen_mlp_gate_up(
                 _p(self.h2), _p(ly["post_attention_layernorm"]), eps, _p(wg), _p(sg), _p(wu), _p(su), I, H,
-                scale_mode(I, sg), _p(self.silu), st), "gate_up"), self._regions(wg, wu)))
+                scale_mode(I, sg), _p(self.silu), st), "gate_up"), self._regions(wg, wu))
             partial_resid(self.silu, ly["down_proj"], self.h2, self.hidden)
         wh, sh = w["lm_head"]
-        plan.append((lambda st: chk(lib.launch_lm_head_argmax(
+        add(lambda st: chk(lib.launch_lm_head_argmax(
             _p(self.hidden), _p(w["norm_f"]), eps, _p(wh), _p(sh), wh.shape[0], H, scale_mode(wh.shape[0], sh),
             w["lm_row_offset"], _p(self.am_ws), _p(self.key), _p(self.token), _p(self.logits), _p(self.pos), st),
-            "lm_head_argmax"), self._regions(wh)))
+            "lm_head_argmax"), self._regions(wh))
+        if p2p:
+            plan.append((lambda st: chk(lib.qwen_token_p2p(table, _p(self.key), _p(self.token), st), "token_p2p"),
+                         []))
+            self.collectives_per_step = 0
+            return plan
         plan.append((lambda st: dist.all_reduce(self.key, op=dist.ReduceOp.MAX, group=self.group), []))
         plan.append((lambda st: chk(lib.qwen_token_from_key(_p(self.key), _p(self.token), st), "token"), []))
         self.collectives_per_step = sum(1 for f, _ in plan if f is allreduce_sum) + 1

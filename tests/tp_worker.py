@@ -13,6 +13,8 @@ single-GPU engine on the same weights:
 * over 10 greedy steps (CUDA graphs): the tokens are identical and the
   logits gathered from the vocabulary shards agree within 5e-2 relative L2,
   the drift of 32 layers of such flips.
+
+QWEN_TP_COLLECTIVE selects the exchange (p2p, the default, or nccl).
 """
 
 import datetime
@@ -37,23 +39,30 @@ def main():
     from qwen35_b200.engine import Qwen35DecodeEngine
     from qwen35_b200.tp import Qwen35TPDecodeEngine
     from qwen35_b200.weights import random_weights
+    collective = os.environ.get("QWEN_TP_COLLECTIVE", "p2p")
     ok = True
     for name, cfg in (("tiny", qwen35_tiny()), ("4b", qwen35_4b())):
         w = random_weights(cfg, seed=21, device="cuda")
         single = Qwen35DecodeEngine(cfg, w, max_seq=64, keep_logits=True)
-        tp = Qwen35TPDecodeEngine(cfg, w, rank, world, max_seq=64, keep_logits=True)
-        # layer by layer, eager (5 launches per layer single, 9 with the all-reduces)
+        tp = Qwen35TPDecodeEngine(cfg, w, rank, world, max_seq=64, keep_logits=True, collective=collective)
+        # layer by layer, eager (5 launches per layer single, tp.launches_per_layer tensor-parallel)
         ps, pt = single._plan_step(), tp._plan_step()
+        nl = tp.launches_per_layer
         stream = torch.cuda.current_stream().cuda_stream
         for e in (single, tp):
             e.token.fill_(101)
         ps[0][0](stream)
         pt[0][0](stream)
+        cur = 1
         for i in range(min(4, cfg.num_hidden_layers)):
             for f, _ in ps[1 + 5 * i:6 + 5 * i]:
                 f(stream)
-            for f, _ in pt[1 + 9 * i:10 + 9 * i]:
+            # with p2p, layer i's output is written by the next launch (layer
+            # i + 1's in_proj or the LM head)
+            end = 1 + nl * (i + 1) + (1 if collective == "p2p" else 0)
+            for f, _ in pt[cur:end]:
                 f(stream)
+            cur = end
             torch.cuda.synchronize()
             err = float((tp.hidden.float() - single.hidden.float()).norm() / single.hidden.float().norm())
             if rank == 0:
@@ -85,10 +94,11 @@ def main():
         if not errs or max(errs) > 5e-2:
             ok = False
         if rank == 0:
-            print(f"{name}: logits rel_l2 per step " + " ".join(f"{e:.1e}" for e in errs), flush=True)
+            print(f"{name} ({collective}): logits rel_l2 per step " + " ".join(f"{e:.1e}" for e in errs), flush=True)
             print(f"{name}: final hidden rel_l2 per step " + " ".join(f"{e:.1e}" for e in herrs), flush=True)
         assert _lib.device_error() == 0
         single.graph = None
+        tp.close()
         tp.graph = None
         del single, tp, w
         torch.cuda.empty_cache()
