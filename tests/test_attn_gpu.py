@@ -84,11 +84,12 @@ def test_layer_mid_attn(lib):
     assert_close(out.cpu(), ref, what="layer_mid_attn")
 
 
-@pytest.mark.parametrize("pos,chunk", [(0, 32), (5, 32), (299, 32), (299, 300), (1000, 64)])
-def test_engine_attn_decode(lib, pos, chunk):
-    """qwen_attn_decode == oracle.ops.attention_decode (gated output)."""
+@pytest.mark.parametrize("pos,chunk,max_seq", [(0, 32, 1088), (5, 32, 1088), (299, 32, 1088), (299, 300, 1088),
+                                               (1000, 64, 1088), (8191, 128, 8192 + 128)])
+def test_engine_attn_decode(lib, pos, chunk, max_seq):
+    """qwen_attn_decode == oracle.ops.attention_decode (gated output), up to the
+    8192-token context of BASELINE config 4 with the engine's split (64 x 128)."""
     g = synth.gen(pos * 3 + chunk)
-    max_seq = 1024 + 64
     nsplit = math.ceil(max_seq / chunk)
     q_all = (torch.randn(NH * 2 * HD, generator=g) * 2).to(BF16)
     k = (torch.randn(NKV * HD, generator=g) * 2).to(BF16)
@@ -125,3 +126,32 @@ def test_engine_attn_decode(lib, pos, chunk):
     assert_close(out.cpu(), ref32, max_rel_err=8e-3, rel_l2_err=4e-3, min_cos=0.9999,
                  what=f"engine attn pos={pos}")
     assert rel_l2(out, ref) < 4e-3
+
+
+def test_engine_attn_decode_rejects_position_past_cache(lib):
+    """A device-side position at or past max_seq is refused by the kernel's own
+    check: nothing is read or written and the device error word says why."""
+    from qwen35_b200 import _lib
+    max_seq, chunk = 64, 32
+    nsplit = 2
+    g = synth.gen(5)
+    q_all = torch.randn(NH * 2 * HD, generator=g).to(BF16).cuda()
+    k = torch.randn(NKV * HD, generator=g).to(BF16).cuda()
+    v = torch.randn(NKV * HD, generator=g).to(BF16).cuda()
+    qn = torch.zeros(HD).cuda()
+    kc = torch.randn(NKV, max_seq, HD, generator=g).to(BF16).cuda()
+    vc = torch.randn(NKV, max_seq, HD, generator=g).to(BF16).cuda()
+    kc0, vc0 = kc.clone(), vc.clone()
+    cos, sin = (t.cuda() for t in ops.rope_tables(max_seq, ROT, 1e7))
+    posd = torch.tensor([max_seq], dtype=torch.int32, device="cuda")
+    ws = torch.empty(NH * nsplit * (HD + 2), dtype=F32, device="cuda")
+    cnt = torch.zeros(NKV, dtype=torch.int32, device="cuda")
+    out = torch.zeros(NH * HD, dtype=BF16, device="cuda")
+    assert _lib.device_error() == 0
+    st = lib.qwen_attn_decode(_p(q_all), _p(k), _p(v), _p(qn), _p(qn), _p(cos), _p(sin), _p(kc), _p(vc), _p(posd),
+                              max_seq, NH, NKV, HD, ROT, 1e-6, chunk, nsplit, _p(ws), _p(cnt), _p(out), P(0))
+    torch.cuda.synchronize()
+    assert st == 0
+    assert _lib.device_error() == 5  # ERR_POS_RANGE (read and cleared)
+    assert torch.equal(kc, kc0) and torch.equal(vc, vc0)
+    assert int(cnt.abs().sum()) == 0 and float(out.float().abs().sum()) == 0.0
