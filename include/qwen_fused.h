@@ -182,6 +182,8 @@ int qwen_mlp_gate_up(const void* h2, const float* norm_w, float eps, const void*
                      const void* w_u, const void* s_u, int N, int K, int K_blk, void* silu_out, cudaStream_t stream);
 /* Full-attention decode with the position on the device: norm, RoPE, KV write,
  * split-KV attention and sigmoid gate (1224-1297, main.py:1001-1059).
+ * The pos + 1 cached positions are spread over nsplit splits (CTAs per KV
+ * head), at least chunk positions each.
  * ws_part: n_heads*nsplit*(head_dim+2) floats; ws_count: n_kv_heads zeroed uints. */
 int qwen_attn_decode(const void* q_all, const void* k_new, const void* v_new, const float* q_norm,
                      const float* k_norm, const float* cos, const float* sin, void* k_cache, void* v_cache,

@@ -8,7 +8,10 @@
 //   gated: out = bf16(out * bf16(sigmoid(gate))).
 //
 // Mapping: one CTA per (KV head, position split).  The CTA handles all G query
-// heads of its KV head, so each K/V row is read once for G heads.  Warps take
+// heads of its KV head, so each K/V row is read once for G heads.  The current
+// context (pos + 1 positions, known only on the device) is spread over the
+// nsplit splits, at least `chunk` positions each, so a graph captured once
+// keeps every split busy as the context grows.  Warps take
 // positions round-robin with a per-warp online softmax; warps are merged in
 // shared memory and splits through an FP32 workspace, the last CTA of each
 // KV head (atomic counter, self-resetting) doing the final merge.
@@ -37,7 +40,7 @@ struct AttnArgs {
   int n_heads, n_kv, rot;
   float eps;
   int prep;
-  int chunk;           // positions per split
+  int chunk;           // at least this many positions per split (see below)
   int nsplit;
   float* ws_part;      // nsplit > 1: [n_heads][nsplit][D + 2]
   unsigned* ws_count;  // nsplit > 1: [n_kv], zero before first use, left zeroed
@@ -157,11 +160,38 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
 #pragma unroll
     for (int e = 0; e < EPL; ++e) o[g][e] = 0.f;
   }
-  const int p0 = split * a.chunk;
-  const int p1 = min(total, p0 + a.chunk);
+  const int chunk = max(a.chunk, (total + a.nsplit - 1) / a.nsplit);
+  const int p0 = split * chunk;
+  const int p1 = min(total, p0 + chunk);
   const bf16* kbase = a.k_cache + (size_t)kh * a.max_seq * D;
   const bf16* vbase = a.v_cache + (size_t)kh * a.max_seq * D;
-  for (int p = p0 + warp; p < p1; p += ATTN_WARPS) {
+  // Each warp takes U consecutive positions at a time and issues all their
+  // K / V row loads (one vector load per lane and row) before using them.
+  constexpr int U = 4;
+  auto load_row = [&](int p, uint32_t (&kr)[EPL / 2], uint32_t (&vr)[EPL / 2]) {
+    const bf16* kp = kbase + (size_t)p * D + lane * EPL;
+    const bf16* vp = vbase + (size_t)p * D + lane * EPL;
+    if constexpr (EPL == 8) {
+      const uint4 k4 = *reinterpret_cast<const uint4*>(kp), v4 = *reinterpret_cast<const uint4*>(vp);
+      kr[0] = k4.x; kr[1] = k4.y; kr[2] = k4.z; kr[3] = k4.w;
+      vr[0] = v4.x; vr[1] = v4.y; vr[2] = v4.z; vr[3] = v4.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPL / 2; ++e) {
+        kr[e] = reinterpret_cast<const uint32_t*>(kp)[e];
+        vr[e] = reinterpret_cast<const uint32_t*>(vp)[e];
+      }
+    }
+  };
+  for (int pb = p0 + warp * U; pb < p1; pb += ATTN_WARPS * U) {
+  uint32_t kb[U][EPL / 2], vb[U][EPL / 2];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    if (pb + u < p1 && !(a.prep && pb + u == pos)) load_row(pb + u, kb[u], vb[u]);
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int p = pb + u;
+    if (p >= p1) continue;  // warp-uniform
     float kx[EPL], vx[EPL];
     if (a.prep && p == pos) {
 #pragma unroll
@@ -170,12 +200,10 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
         vx[e] = kv_sm[D + lane * EPL + e];
       }
     } else {
-      const bf16* kp = kbase + (size_t)p * D + lane * EPL;
-      const bf16* vp = vbase + (size_t)p * D + lane * EPL;
 #pragma unroll
       for (int e = 0; e < EPL; e += 2) {
-        const float2 kf = bf2x_to_f2(*reinterpret_cast<const uint32_t*>(kp + e));
-        const float2 vf = bf2x_to_f2(*reinterpret_cast<const uint32_t*>(vp + e));
+        const float2 kf = bf2x_to_f2(kb[u][e / 2]);
+        const float2 vf = bf2x_to_f2(vb[u][e / 2]);
         kx[e] = kf.x;
         kx[e + 1] = kf.y;
         vx[e] = vf.x;
@@ -196,6 +224,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
       l[g] = l[g] * eo + en;
       m[g] = nm;
     }
+  }
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -251,7 +280,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const int n_active = (total + a.chunk - 1) / a.chunk;
+  const int n_active = (total + chunk - 1) / chunk;
   for (int idx = threadIdx.x; idx < G * D; idx += ATTN_WARPS * 32) {
     const int g = idx / D, d = idx % D;
     const int h = kh * G + g;

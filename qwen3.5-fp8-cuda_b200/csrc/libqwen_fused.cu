@@ -728,7 +728,7 @@ int qwen_attn_decode(const void* q_all, const void* k_new, const void* v_new, co
   a.ws_count = ws_count;
   a.out = static_cast<bf16*>(out);
   a.pf = take_prefetch();
-  if (!pos || (long long)chunk * nsplit < max_seq) return record(cudaErrorInvalidValue);
+  if (!pos || chunk < 1 || nsplit < 1) return record(cudaErrorInvalidValue);
   return record(launch_attn(a, head_dim, stream, engine_pdl()));
 }
 

@@ -92,12 +92,13 @@ class Qwen35DecodeEngine:
         cos, sin = rope_tables(self.max_seq, cfg.rotary_dim, cfg.rope_theta)
         self.cos, self.sin = cos.to(dev), sin.to(dev)
 
-        # Split-KV attention: chunk positions per CTA.
-        if attn_chunk is None:
-            nsplit = min(64, max(1, math.ceil(self.max_seq / 32)))
-            attn_chunk = math.ceil(self.max_seq / nsplit)
-        self.attn_chunk = int(attn_chunk)
-        self.attn_nsplit = math.ceil(self.max_seq / self.attn_chunk)
+        # Split-KV attention: one wave of CTAs (KV heads x splits <= SMs); the
+        # kernel spreads the current context over the splits, at least
+        # attn_chunk positions each.
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.attn_chunk = int(attn_chunk) if attn_chunk is not None else 32
+        self.attn_nsplit = max(1, min(sms // max(1, cfg.num_key_value_heads),
+                                      math.ceil(self.max_seq / self.attn_chunk)))
         self.attn_ws = empty(cfg.num_attention_heads * self.attn_nsplit * (cfg.head_dim + 2), f32)
         self.attn_cnt = torch.zeros(cfg.num_key_value_heads, dtype=torch.int32, device=dev)
 
