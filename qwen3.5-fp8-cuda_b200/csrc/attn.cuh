@@ -281,19 +281,58 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
   if (!s_last) return;
   __threadfence();
   const int n_active = (total + chunk - 1) / chunk;
+  // Split weights: warp g handles head g with its lanes over the splits
+  // (the per-warp output area holds f_s = exp(m_s - M)); then every thread
+  // adds its (head, channel) over the splits with 8 split rows in flight.
+  float* fac = wo;
+  constexpr int FCAP = ATTN_WARPS * D;  // splits per head that fit
+  const bool fits = n_active <= FCAP;
+  if (fits) {
+    for (int g = warp; g < G; g += ATTN_WARPS) {
+      const float* base = a.ws_part + (size_t)(kh * G + g) * nsplit * (D + 2);
+      float M = -INFINITY;
+      for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(base + s * (D + 2)));
+      M = warp_max(M);
+      float L = 0.f;
+      for (int s = lane; s < n_active; s += 32) {
+        const float ms = __ldcg(base + s * (D + 2));
+        const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+        L += __ldcg(base + s * (D + 2) + 1) * f;
+        fac[g * FCAP + s] = f;
+      }
+      L = warp_sum(L);
+      if (lane == 0) wl[g] = L;
+    }
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * D; idx += ATTN_WARPS * 32) {
     const int g = idx / D, d = idx % D;
     const int h = kh * G + g;
     const float* base = a.ws_part + (size_t)h * nsplit * (D + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(base + s * (D + 2)));
-    float Ls = 0.f, Os = 0.f;
-    for (int s = 0; s < n_active; ++s) {
-      const float ms = __ldcg(base + s * (D + 2));
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      Ls += __ldcg(base + s * (D + 2) + 1) * f;
-      Os += __ldcg(base + s * (D + 2) + 2 + d) * f;
+    float Os = 0.f, Ls;
+    if (fits) {
+      const float* fg = fac + g * FCAP;
+      int s = 0;
+      for (; s + 8 <= n_active; s += 8) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = __ldcg(base + (s + j) * (D + 2) + 2 + d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) Os = fmaf(o[j], fg[s + j], Os);
+      }
+      for (; s < n_active; ++s) Os = fmaf(__ldcg(base + s * (D + 2) + 2 + d), fg[s], Os);
+      Ls = wl[g];
+    } else {
+      float M = -INFINITY;
+      for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(base + s * (D + 2)));
+      Ls = 0.f;
+      for (int s = 0; s < n_active; ++s) {
+        const float ms = __ldcg(base + s * (D + 2));
+        if (ms == -INFINITY) continue;
+        const float f = expf(ms - M);
+        Ls += __ldcg(base + s * (D + 2) + 1) * f;
+        Os += __ldcg(base + s * (D + 2) + 2 + d) * f;
+      }
     }
     bf16 ob = f2bf(Os * (1.0f / Ls));
     if (a.gate) {
