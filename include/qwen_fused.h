@@ -140,6 +140,16 @@ int qwen_gdn_in_proj(const void* hidden, const float* norm_w, float eps, int K, 
 int qwen_gdn_decode(const void* qkv, const float* g, const void* beta, float* state, const void* z,
                     const void* norm_w, float eps, void* out, int n_k_heads, int n_v_heads, int head_dim,
                     cudaStream_t stream);
+/* GatedDeltaNet recurrent step writing the un-normed core output (value
+ * columns of a head over 4 CTAs); the gated norm then runs in the next
+ * GEMV's prologue after qwen_set_gated_input.  No counterpart in the
+ * reference (its gated norm is a separate kernel, 592-618). */
+int qwen_gdn_decode_core(const void* qkv, const float* g, const void* beta, float* state, void* core_out,
+                         int n_k_heads, int n_v_heads, int head_dim, cudaStream_t stream);
+/* The next launch without a prologue on this host thread (qwen_linear_resid,
+ * qwen_linear_partial, qwen_linear_partial_p2p) applies RMSNormGated per
+ * 128-wide head to its x: z like x, norm_w [128] BF16 (main.py:1152-1159). */
+int qwen_set_gated_input(const void* z, const void* norm_w, float eps);
 /* y = bf16(res + bf16(W x)): o_proj / out_proj / down with the residual add (553-559). */
 int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K, int K_blk, const void* res, void* y,
                       cudaStream_t stream);

@@ -13,6 +13,9 @@
 //    prediction and the update;
 //  * KG thread groups split the key dimension, so a head runs D*KG threads;
 //  * value head h reads key head h / rep directly (no repeat_interleave copy);
+//  * without the fused epilogue the D value columns of a head are split over
+//    VS CTAs (the columns are independent), which spreads the state traffic
+//    over VS times more SMs;
 //  * optional fused epilogue: the default decode path's RMSNormGated
 //    (main.py:1152-1159): out = bf16(bf16(bf16(o*rsqrt(mean(o^2)+eps)) * w) * bf16(silu(z)))
 //    with o = bf16(core).
@@ -38,16 +41,19 @@ struct GdnArgs {
   L2Prefetch pf;       // weights of the next launch (see common.cuh)
 };
 
-template <int D, int KG>
-__global__ void __launch_bounds__(D * KG) gdn_decode_kernel(const __grid_constant__ GdnArgs a) {
-  constexpr int NT = D * KG;
+template <int D, int KG, int VS>
+__global__ void __launch_bounds__(D * KG / VS) gdn_decode_kernel(const __grid_constant__ GdnArgs a) {
+  static_assert(VS <= KG, "q / k loads need at least D threads");
+  constexpr int DC = D / VS;  // value columns of this CTA
+  constexpr int NT = DC * KG;
   constexpr int KS = D / KG;  // key rows per thread
   __shared__ float qs[D], ks[D];
-  __shared__ float red[KG][D];
+  __shared__ float red[KG][DC];
   __shared__ float wsum[NT / 32 + 1];
   const int h = blockIdx.x;
   const int tid = threadIdx.x;
-  const int d = tid % D, grp = tid / D;
+  const int dl = tid % DC, grp = tid / DC;
+  const int d = blockIdx.y * DC + dl;
   const int lane = tid & 31, warp = tid >> 5;
 
   if (tid == 0) pdl_trigger();
@@ -95,11 +101,11 @@ __global__ void __launch_bounds__(D * KG) gdn_decode_kernel(const __grid_constan
   float pred = 0.f;
 #pragma unroll
   for (int i = 0; i < KS; ++i) pred += s[i] * decay * ks[grp * KS + i];
-  red[grp][d] = pred;
+  red[grp][dl] = pred;
   __syncthreads();
   float ptot = 0.f;
 #pragma unroll
-  for (int gI = 0; gI < KG; ++gI) ptot += red[gI][d];
+  for (int gI = 0; gI < KG; ++gI) ptot += red[gI][dl];
   const float delta = (bf2f(a.v[(size_t)h * D + d]) - ptot) * beta;
   __syncthreads();  // everyone has read red before it is reused
 
@@ -110,15 +116,15 @@ __global__ void __launch_bounds__(D * KG) gdn_decode_kernel(const __grid_constan
     S[(size_t)(grp * KS + i) * D + d] = u;
     o += u * qs[grp * KS + i];
   }
-  red[grp][d] = o;
+  red[grp][dl] = o;
   __syncthreads();
   if (grp != 0) return;
   float ot = 0.f;
 #pragma unroll
-  for (int gI = 0; gI < KG; ++gI) ot += red[gI][d];
+  for (int gI = 0; gI < KG; ++gI) ot += red[gI][dl];
   const bf16 core = f2bf(ot);
   bf16* out = a.out + (size_t)h * D + d;
-  if (!a.gated) {
+  if (VS > 1 || !a.gated) {
     *out = core;
     return;
   }
@@ -142,8 +148,11 @@ static inline cudaError_t launch_gdn(const GdnArgs& a, int n_heads, int head_dim
   if (n_heads <= 0) return cudaSuccess;
   if (!a.q || !a.k || !a.v || !a.g || !a.beta || !a.state || !a.out || a.rep <= 0) return cudaErrorInvalidValue;
   if (a.gated && (!a.z || !a.norm_w)) return cudaErrorInvalidValue;
+  // The fused gated norm needs a whole head per CTA; the core output alone is
+  // split over 4 CTAs per head.
+  const int vs = a.gated ? 1 : 4;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(n_heads);
+  cfg.gridDim = dim3(n_heads, vs);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -152,11 +161,13 @@ static inline cudaError_t launch_gdn(const GdnArgs& a, int n_heads, int head_dim
   cfg.numAttrs = 1;
   switch (head_dim) {
     case 64:
-      cfg.blockDim = dim3(64 * 4);
-      return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<64, 4>, a);
+      cfg.blockDim = dim3(64 * 4 / vs);
+      return vs == 1 ? cudaLaunchKernelEx(&cfg, gdn_decode_kernel<64, 4, 1>, a)
+                     : cudaLaunchKernelEx(&cfg, gdn_decode_kernel<64, 4, 4>, a);
     case 128:
-      cfg.blockDim = dim3(128 * 4);
-      return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<128, 4>, a);
+      cfg.blockDim = dim3(128 * 4 / vs);
+      return vs == 1 ? cudaLaunchKernelEx(&cfg, gdn_decode_kernel<128, 4, 1>, a)
+                     : cudaLaunchKernelEx(&cfg, gdn_decode_kernel<128, 4, 4>, a);
     default:  // head dims of the Qwen3.5 family are 128 (64 kept for small tests)
       return cudaErrorInvalidValue;
   }

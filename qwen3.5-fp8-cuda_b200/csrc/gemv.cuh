@@ -68,6 +68,7 @@ enum GemvPro : int {
   PRO_RMSNORM = 1,      // x <- bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))
   PRO_ADD_RMSNORM = 2,  // h2 <- bf16(x + x2) (stored by CTA 0); x <- rmsnorm(h2)
   PRO_P2P_RMSNORM = 3,  // h2 <- bf16(x + bf16(sum of the ranks' partials, p2p)) (stored by CTA 0); x <- rmsnorm(h2)
+  PRO_GATED_NORM = 4,   // per 128-block (one GatedDeltaNet head): x <- RMSNormGated(x, z) (gz, gw, eps)
 };
 
 struct GemvSeg {
@@ -109,6 +110,8 @@ struct GemvArgs {
   int* pos_inc;                    // optional: ++*pos_inc by the argmax finaliser
   L2Prefetch pf;                   // weights of the next launch, pulled into L2 while this one runs
   const P2PTable* p2p;             // PRO_P2P_RMSNORM: the tensor-parallel exchange of this round
+  const bf16* gz;                  // PRO_GATED_NORM: gate z, same layout as x
+  const bf16* gw;                  // PRO_GATED_NORM: norm weight of one 128-wide head
   GemvSeg seg[GEMV_MAX_SEG];
 };
 

@@ -413,7 +413,7 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
     const cudaError_t e = wide ? gemv_tcw_run(a, f32_scales, st, pdl) : gemv_tc_run(a, f32_scales, st, pdl);
     if (e != cudaErrorNotSupported) return e;
   }
-  if (a.pro == PRO_P2P_RMSNORM) return cudaErrorNotSupported;  // tcgen05 kernels only
+  if (a.pro == PRO_P2P_RMSNORM || a.pro == PRO_GATED_NORM) return cudaErrorNotSupported;  // tcgen05 kernels only
   if (npair != 0 && npair != a.nseg) mma_ok = false;
   if (mma_ok && (a.K / 128 + GEMV_WARPS - 1) / GEMV_WARPS > 32) mma_ok = false;  // K > 32768
   if (mma_ok) {

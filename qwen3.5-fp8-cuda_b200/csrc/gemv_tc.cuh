@@ -262,6 +262,9 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
       if (i < nch) {
         v[j] = __ldg(reinterpret_cast<const uint4*>(xin) + i);
         if (a.pro == PRO_ADD_RMSNORM) r[j] = __ldg(reinterpret_cast<const uint4*>(a.x2) + i);
+        // gated norm: z of the slice's blocks in the same round trip as x
+        if (a.pro == PRO_GATED_NORM && (i >> 4) >= kb0 && (i >> 4) < kb0 + nxb)
+          r[j] = __ldg(reinterpret_cast<const uint4*>(a.gz) + i);
       }
     }
 #pragma unroll
@@ -286,14 +289,18 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
         ss = fmaf(f.y, f.y, ss);
       }
       const int b = i >> 4;  // 16 chunks of 8 elements per 128-block
-      if (b >= kb0 && b < kb0 + nxb) reinterpret_cast<uint4*>(stg)[i - kb0 * 16] = v[j];
+      if (b >= kb0 && b < kb0 + nxb) {
+        reinterpret_cast<uint4*>(stg)[i - kb0 * 16] = v[j];
+        // gated norm: z staged where the RMSNorm weights would be
+        if (a.pro == PRO_GATED_NORM) reinterpret_cast<uint4*>(const_cast<float*>(nws))[i - kb0 * 16] = r[j];
+      }
     }
   }
   ss = warp_sum(ss);
   if (lane == 0) red[w] = ss;
   named_bar(1, NT);
   float rms = 1.f;
-  if (a.pro != PRO_NONE) {
+  if (a.pro != PRO_NONE && a.pro != PRO_GATED_NORM) {
     float tot = 0.f;
 #pragma unroll
     for (int i = 0; i < NW; ++i) tot += red[i];
@@ -319,7 +326,26 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
         v[2] = bfround(v[2] + g23.x); v[3] = bfround(v[3] + g23.y);
       }
     }
-    if (a.pro != PRO_NONE) {
+    if (a.pro == PRO_GATED_NORM) {
+      // RMSNormGated over this 128-wide block (one GatedDeltaNet value head),
+      // the default decode path's rounding points (main.py:1152-1159):
+      // bf16(bf16(bf16(c * rsqrt(mean(c^2) + eps)) * w) * bf16(silu(z)))
+      float cs = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+      cs = warp_sum(cs);
+      const float r = rsqrtf(cs / 128.0f + a.eps);
+      // z staged in pass 1, the norm weight before griddepcontrol.wait
+      const uint2 zr = reinterpret_cast<const uint2*>(nws)[(b - kb0) * 32 + lane];
+      const uint2 wr = reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(nws) + nxb * 256)[lane];
+      const float2 z01 = bf2x_to_f2(zr.x), z23 = bf2x_to_f2(zr.y);
+      const float2 w01 = bf2x_to_f2(wr.x), w23 = bf2x_to_f2(wr.y);
+      const float zv[4] = {z01.x, z01.y, z23.x, z23.y}, wv[4] = {w01.x, w01.y, w23.x, w23.y};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float t = bfround(bfround(v[q] * r) * wv[q]);
+        const float zs = bfround(zv[q] / (1.0f + expf(-zv[q])));
+        v[q] = bfround(t * zs);
+      }
+    } else if (a.pro != PRO_NONE) {
       const float4 wn = in_slice ? reinterpret_cast<const float4*>(nws)[(b - kb0) * 32 + lane]
                                  : __ldg(reinterpret_cast<const float4*>(a.norm_w + k0));
       const float wv[4] = {wn.x, wn.y, wn.z, wn.w};
@@ -442,11 +468,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       p_has = p_next();
     }
   }
-  if (warp >= 2 && a.pro != PRO_NONE) {
+  if (warp >= 2 && a.pro != PRO_NONE && a.pro != PRO_GATED_NORM) {
     // RMSNorm weights of this CTA's slice (static data: before griddepcontrol.wait)
     float4* nws = reinterpret_cast<float4*>(gbase + L.nw_off);
     const float4* src = reinterpret_cast<const float4*>(a.norm_w + ckb0 * 128);
     for (int o = threadIdx.x - 64; o < cnxb * 32; o += 192) nws[o] = __ldg(src + o);
+  }
+  if (warp >= 2 && a.pro == PRO_GATED_NORM && threadIdx.x - 64 < 16) {
+    // gated-norm weight (one head, static) after the staged z
+    reinterpret_cast<uint4*>(gbase + L.nw_off + cnxb * 256)[threadIdx.x - 64] =
+        __ldg(reinterpret_cast<const uint4*>(a.gw) + (threadIdx.x - 64));
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"

@@ -193,11 +193,14 @@ __global__ void __launch_bounds__(TW_THREADS, 2)
     }
   }
   if (warp >= 2) {
-    if (a.pro != PRO_NONE) {
+    if (a.pro != PRO_NONE && a.pro != PRO_GATED_NORM) {
       float4* nws = reinterpret_cast<float4*>(gbase + L.nw_off);
       const float4* src = reinterpret_cast<const float4*>(a.norm_w + ckb0 * 128);
       for (int o = threadIdx.x - 64; o < cnxb * 32; o += 192) nws[o] = __ldg(src + o);
     }
+    if (a.pro == PRO_GATED_NORM && threadIdx.x - 64 < 16)  // gated-norm weight after the staged z
+      reinterpret_cast<uint4*>(gbase + L.nw_off + cnxb * 256)[threadIdx.x - 64] =
+          __ldg(reinterpret_cast<const uint4*>(a.gw) + (threadIdx.x - 64));
     tc_x_zero<TW_XBLK>(cnxb, gbase + L.xa_off);
   }
   if (warp == 1) {

@@ -40,6 +40,26 @@ thread_local const void* g_p2p_table = nullptr;
 thread_local const void* g_p2p_res = nullptr;
 thread_local int g_p2p_n = 0;
 
+// GatedDeltaNet gated norm of the next PRO_NONE launch on this host thread
+// (set by qwen_set_gated_input, consumed and cleared by that launch).
+thread_local const void* g_gz = nullptr;
+thread_local const void* g_gw = nullptr;
+thread_local float g_geps = 0.f;
+
+inline cudaError_t take_gated_input(GemvArgs& a) {
+  if (!g_gz) return cudaSuccess;
+  const void* z = g_gz;
+  const void* w = g_gw;
+  const float eps = g_geps;
+  g_gz = g_gw = nullptr;
+  if (a.pro != PRO_NONE || a.K % 128 != 0 || a.xn_out || a.h2_out || a.x_row) return cudaErrorInvalidValue;
+  a.pro = PRO_GATED_NORM;
+  a.gz = static_cast<const bf16*>(z);
+  a.gw = static_cast<const bf16*>(w);
+  a.eps = eps;
+  return cudaSuccess;
+}
+
 inline cudaError_t take_p2p_input(GemvArgs& a) {
   if (!g_p2p_table) return cudaSuccess;
   const void* t = g_p2p_table;
@@ -147,6 +167,17 @@ void qwen_set_pdl(int enable) { g_pdl_enabled = enable; }
 // The next RMSNorm-prologue launch on this host thread takes its input from
 // the tensor-parallel exchange `table` (n-element partial sums) plus the
 // residual `res` (see take_p2p_input).
+// The next launch without a prologue on this host thread (an out_proj after
+// qwen_gdn_decode_core) applies the GatedDeltaNet gated RMSNorm to its x per
+// 128-wide head: z [like x], norm weight [128] BF16.
+int qwen_set_gated_input(const void* z, const void* norm_w, float eps) {
+  if (!z || !norm_w) return record(cudaErrorInvalidValue);
+  g_gz = z;
+  g_gw = norm_w;
+  g_geps = eps;
+  return 0;
+}
+
 int qwen_set_p2p_input(const void* table, const void* res, int n) {
   if (!table || !res || n <= 0) return record(cudaErrorInvalidValue);
   g_p2p_table = table;
@@ -524,6 +555,27 @@ int qwen_gdn_decode(const void* qkv, const float* g, const void* beta, float* st
   return record(launch_gdn(a, n_v_heads, head_dim, stream, engine_pdl()));
 }
 
+// GatedDeltaNet recurrent step writing the un-normed core output (the gated
+// norm then runs in the next GEMV's prologue, qwen_set_gated_input); the
+// value columns of a head are split over 4 CTAs.
+int qwen_gdn_decode_core(const void* qkv, const float* g, const void* beta, float* state, void* core_out,
+                         int n_k_heads, int n_v_heads, int head_dim, cudaStream_t stream) {
+  if (n_k_heads <= 0 || n_v_heads % n_k_heads) return record(cudaErrorInvalidValue);
+  const bf16* base = static_cast<const bf16*>(qkv);
+  GdnArgs a = {};
+  a.q = base;
+  a.k = base + (size_t)n_k_heads * head_dim;
+  a.v = base + (size_t)2 * n_k_heads * head_dim;
+  a.g = g;
+  a.beta = static_cast<const bf16*>(beta);
+  a.state = state;
+  a.out = static_cast<bf16*>(core_out);
+  a.rep = n_v_heads / n_k_heads;
+  a.gated = 0;
+  a.pf = take_prefetch();
+  return record(launch_gdn(a, n_v_heads, head_dim, stream, engine_pdl()));
+}
+
 // y = bf16(res + bf16(W x)) (o_proj / out_proj / down with the residual add).
 int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K, int K_blk, const void* res, void* y,
                       cudaStream_t stream) {
@@ -532,6 +584,7 @@ int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K,
   a.seg[0] = seg(w, s, y, N, K_blk, EPI_RESID);
   a.seg[0].aux0 = res;
   a.pf = take_prefetch();
+  if (cudaError_t ge = take_gated_input(a)) return record(ge);
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -544,6 +597,7 @@ int qwen_linear_partial(const void* x, const void* w, const void* s, int N, int 
   a.nseg = 1;
   a.seg[0] = seg(w, s, y, N, K_blk, EPI_F32);
   a.pf = take_prefetch();
+  if (cudaError_t ge = take_gated_input(a)) return record(ge);
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 
@@ -657,6 +711,7 @@ int qwen_linear_partial_p2p(const void* x, const void* w, const void* s, int N, 
   a.seg[0] = seg(w, s, nullptr, N, K_blk, EPI_F32_P2P);
   a.seg[0].aux0 = table;
   a.pf = take_prefetch();
+  if (cudaError_t ge = take_gated_input(a)) return record(ge);
   return record(gemv_run(a, false, stream, engine_pdl()));
 }
 

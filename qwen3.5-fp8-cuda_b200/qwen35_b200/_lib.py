@@ -78,6 +78,8 @@ NEW_FUSED = {
     "qwen_resid_add_p2p": (I, [P, P, P, I, P]),
     "qwen_token_p2p": (I, [P, P, P, P]),
     "qwen_set_p2p_input": (I, [P, P, I]),
+    "qwen_gdn_decode_core": (I, [P, P, P, P, P, I, I, I, P]),
+    "qwen_set_gated_input": (I, [P, P, F]),
 }
 NEW_FP8 = {
     "qwen_fp8_last_error": (I, []),

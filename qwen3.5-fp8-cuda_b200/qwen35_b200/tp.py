@@ -269,17 +269,23 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
                     return inner(st)
             plan.append((launch, regions))
 
-        def partial_resid(x, wt, res, out):
+        def partial_resid(x, wt, res, out, gated=None):
+            """gated = (z, norm_w): x is a GatedDeltaNet core output whose gated
+            norm runs in this GEMV's prologue."""
             wo, so = wt
+
+            def pre():
+                if gated is not None:
+                    chk(lib.qwen_set_gated_input(_p(gated[0]), _p(gated[1]), eps), "gated_input")
             if p2p:
-                plan.append((lambda st: chk(lib.qwen_linear_partial_p2p(
+                plan.append((lambda st: (pre(), chk(lib.qwen_linear_partial_p2p(
                     _p(x), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so), table, st),
-                    "linear_partial_p2p"), self._regions(wo)))
+                    "linear_partial_p2p")), self._regions(wo)))
                 pending.append(res)  # the consumer writes bf16(res + sum) to `out`, its x
                 return
-            plan.append((lambda st: chk(lib.qwen_linear_partial(
+            plan.append((lambda st: (pre(), chk(lib.qwen_linear_partial(
                 _p(x), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
-                _p(self.partial), st), "linear_partial"), self._regions(wo)))
+                _p(self.partial), st), "linear_partial")), self._regions(wo)))
             plan.append((allreduce_sum, []))
             plan.append((lambda st: chk(lib.qwen_resid_add_f32(_p(res), _p(self.partial), _p(out), H, st),
                                         "resid_add"), []))
@@ -311,11 +317,19 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
                                  _p(self.z), _p(wa), _p(sa), _p(wb), _p(sb), wa.shape[0], _p(ly["A_log"]),
                                  _p(ly["dt_bias"]), _p(self.g), _p(self.beta), st), "gdn_in_proj"),
                              self._regions(wqkv, wz, wa, wb))
-                plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_gdn_decode(
-                    _p(self.qkv_conv), _p(self.g), _p(self.beta), _p(self.state[i]), _p(self.z), _p(ly["norm_w"]),
-                    eps, _p(self.attn_out), cfg.linear_num_key_heads, cfg.linear_num_value_heads,
-                    cfg.linear_value_head_dim, st), "gdn_decode"), []))
-                partial_resid(self.attn_out, ly["out_proj"], self.hidden, self.h2)
+                if self.gdn_split:
+                    plan.append((lambda st, i=i: chk(lib.qwen_gdn_decode_core(
+                        _p(self.qkv_conv), _p(self.g), _p(self.beta), _p(self.state[i]), _p(self.attn_out),
+                        cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_value_head_dim, st),
+                        "gdn_decode_core"), []))
+                    partial_resid(self.attn_out, ly["out_proj"], self.hidden, self.h2,
+                                  gated=(self.z, ly["norm_w"]))
+                else:
+                    plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_gdn_decode(
+                        _p(self.qkv_conv), _p(self.g), _p(self.beta), _p(self.state[i]), _p(self.z),
+                        _p(ly["norm_w"]), eps, _p(self.attn_out), cfg.linear_num_key_heads,
+                        cfg.linear_num_value_heads, cfg.linear_value_head_dim, st), "gdn_decode"), []))
+                    partial_resid(self.attn_out, ly["out_proj"], self.hidden, self.h2)
             (wg, sg), (wu, su) = ly["gate_proj"], ly["up_proj"]
             add(lambda st, ly=ly, wg=wg, sg=sg, wu=wu, su=su: chk(lib.qwen_mlp_gate_up(
                 _p(self.h2), _p(ly["post_attention_layernorm"]), eps, _p(wg), _p(sg), _p(wu), _p(su), I, H,

@@ -103,9 +103,13 @@ def test_gates_and_gated_norm_reference_kernels(lib):
     assert_close(out.cpu(), ref32, what="gated norm (fp32 form)")
 
 
-def test_gdn_layer_engine_kernels(lib):
+@pytest.mark.parametrize("split", [False, True], ids=["fused_norm", "norm_in_out_proj"])
+def test_gdn_layer_engine_kernels(lib, split):
     """qwen_gdn_in_proj + qwen_gdn_decode + qwen_linear_resid on a full-size
-    GDN layer against oracle.model's layer (main.py:1064-1163 semantics)."""
+    GDN layer against oracle.model's layer (main.py:1064-1163 semantics).
+    split: qwen_gdn_decode_core (value columns over 4 CTAs per head) and the
+    gated norm in out_proj's prologue (qwen_set_gated_input), as the engine
+    runs it."""
     from qwen35_b200.config import qwen35_4b
     cfg = qwen35_4b()
     g = synth.gen(6)
@@ -155,9 +159,14 @@ def test_gdn_layer_engine_kernels(lib):
                               _p(z_out), _p(dev["a"][0]), _p(dev["a"][1]), _p(dev["b"][0]), _p(dev["b"][1]), HV,
                               _p(dal), _p(ddt), _p(g_out), _p(b_out), P(0))
     assert st == 0
-    st = lib.qwen_gdn_decode(_p(qkv_out), _p(g_out), _p(b_out), _p(sd), _p(z_out), _p(dnw), 1e-6,
-                             _p(gated_out), HK, HV, D, P(0))
-    assert st == 0
+    if split:
+        st = lib.qwen_gdn_decode_core(_p(qkv_out), _p(g_out), _p(b_out), _p(sd), _p(gated_out), HK, HV, D, P(0))
+        assert st == 0
+        assert lib.qwen_set_gated_input(_p(z_out), _p(dnw), ctypes.c_float(1e-6)) == 0
+    else:
+        st = lib.qwen_gdn_decode(_p(qkv_out), _p(g_out), _p(b_out), _p(sd), _p(z_out), _p(dnw), 1e-6,
+                                 _p(gated_out), HK, HV, D, P(0))
+        assert st == 0
     st = lib.qwen_linear_resid(_p(gated_out), _p(dev["out"][0]), _p(dev["out"][1]), Hh, vd, 32, _p(dh), _p(y), P(0))
     assert st == 0
     torch.cuda.synchronize()
