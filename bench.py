@@ -481,6 +481,7 @@ def run_ours(args):
         except Exception as exc:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": repr(exc)[:200]}
     eng.graph = None
+    eng.graph_io = None
     if world > 1:
         eng.close()
         dist.barrier()

@@ -160,6 +160,11 @@ int qwen_linear_partial(const void* x, const void* w, const void* s, int N, int 
                         cudaStream_t stream);
 /* y = bf16(res + bf16(v)) for n elements, v the all-reduced partial sums. */
 int qwen_resid_add_f32(const void* res, const float* v, void* y, int n, cudaStream_t stream);
+/* Writes {*token, ++*seq} to host_out (pinned host memory the device can
+ * write, e.g. cudaHostAlloc under unified addressing): the token first, the
+ * sequence number after a system-scope fence, so a host thread polling the
+ * sequence number reads the matching token.  No counterpart in the reference. */
+int qwen_publish_token(const long long* token, long long* host_out, unsigned long long* seq, cudaStream_t stream);
 /* token = the greedy token id encoded in an all-reduced packed argmax key. */
 int qwen_token_from_key(const long long* key, long long* token, cudaStream_t stream);
 /* Tensor parallelism without a library collective: the partial sums and the

@@ -617,6 +617,22 @@ int qwen_resid_add_f32(const void* res, const float* v, void* y, int n, cudaStre
                                    static_cast<bf16*>(y), n));
 }
 
+// Copies the step's token to host-mapped pinned memory host_out[0..1] =
+// {token, sequence number} (see publish_token_kernel).
+int qwen_publish_token(const long long* token, long long* host_out, unsigned long long* seq, cudaStream_t stream) {
+  if (!token || !host_out || !seq) return record(cudaErrorInvalidValue);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = engine_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return record(cudaLaunchKernelEx(&cfg, publish_token_kernel, token, host_out, seq));
+}
+
 // token = greedy token encoded in an all-reduced packed argmax key.
 int qwen_token_from_key(const long long* key, long long* token, cudaStream_t stream) {
   if (!key || !token) return record(cudaErrorInvalidValue);

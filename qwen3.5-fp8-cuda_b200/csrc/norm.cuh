@@ -101,6 +101,20 @@ __global__ void resid_add_f32_kernel(const bf16* __restrict__ res, const float* 
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) y[i] = f2bf(bf2f(res[i]) + bfround(v[i]));
 }
+// Publishes the step's token to mapped pinned host memory: host_out[0] =
+// token, then (after a system-scope fence) host_out[1] = ++*seq, so a host
+// thread that sees the new sequence number reads the matching token.
+__global__ void publish_token_kernel(const long long* __restrict__ token, volatile long long* host_out,
+                                     unsigned long long* seq) {
+  pdl_wait();
+  if (threadIdx.x == 0) pdl_trigger();
+  if (threadIdx.x != 0) return;
+  const unsigned long long s = *seq + 1ull;
+  *seq = s;
+  host_out[0] = *token;
+  __threadfence_system();
+  host_out[1] = (long long)s;
+}
 // token = index part of the all-reduced packed argmax key.
 __global__ void token_from_key_kernel(const unsigned long long* key, long long* token) {
   pdl_wait();

@@ -68,6 +68,7 @@ NEW_FUSED = {
     "qwen_linear_partial": (I, [P, P, P, I, I, I, P, P]),
     "qwen_resid_add_f32": (I, [P, P, P, I, P]),
     "qwen_token_from_key": (I, [P, P, P]),
+    "qwen_publish_token": (I, [P, P, P, P]),
     "qwen_p2p_create": (I, [I, I, P, P]),
     "qwen_p2p_open": (I, [P, P]),
     "qwen_p2p_close": (I, [P]),

@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import time
 
 import torch
 
@@ -120,8 +121,15 @@ class Qwen35DecodeEngine:
                 self.state[i] = torch.zeros(cfg.linear_num_value_heads, cfg.linear_key_head_dim,
                                             cfg.linear_value_head_dim, dtype=f32, device=dev)
         self.graph = None
+        self.graph_io = None
         self._h_tok = torch.zeros(1, dtype=torch.int64, pin_memory=True)
         self._h_out = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+        # decode() I/O: [0] input token, [2] output token, [3] step sequence number
+        # (pinned; the step graph copies [0] in and its last kernel writes [2], [3])
+        self._io = torch.zeros(4, dtype=torch.int64, pin_memory=True)
+        self._io_np = self._io.numpy()
+        self._dseq = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._seq = 0
         self.launches_per_step = 0
         self.kernels_per_step = 0
 
@@ -262,10 +270,21 @@ class Qwen35DecodeEngine:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             self._launch_step(s.cuda_stream)
+        # decode(): the same step with its host I/O inside the graph: the input
+        # token copied in from pinned memory, the output token and a sequence
+        # number written to pinned memory by the last kernel
+        gio = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gio, stream=s):
+            self.token.copy_(self._io[0:1], non_blocking=True)
+            self._launch_step(s.cuda_stream)
+            _lib.check(self.lib.qwen_publish_token(_p(self.token), P(self._io.data_ptr() + 16), _p(self._dseq),
+                                                   P(s.cuda_stream)), "qwen_publish_token")
         torch.cuda.synchronize(self.device)
         for t, v in zip(self._mutable(), saved):
             t.copy_(v)
         self.graph = g
+        self.graph_io = gio
+        self._seq = int(self._dseq.item())
         return g
 
     def _mutable(self):
@@ -282,7 +301,26 @@ class Qwen35DecodeEngine:
     # ------------------------------------------------------------------
     # Public API: host token in, host token out (one step end to end).
     def decode(self, token: int) -> int:
-        """Feed ``token`` at the current position; return the greedy next token."""
+        """Feed ``token`` at the current position; return the greedy next token.
+
+        With a captured graph the step's I/O is part of it: the token goes in
+        from pinned memory and the host polls the pinned sequence number the
+        last kernel writes (bounded: after 2 s it synchronises and raises).
+        """
+        if self.graph_io is not None:
+            io = self._io_np
+            io[0] = int(token)
+            expect = self._seq + 1
+            self.graph_io.replay()
+            if io[3] != expect:
+                t0 = time.perf_counter()
+                while io[3] != expect:
+                    if time.perf_counter() - t0 > 2.0:
+                        torch.cuda.current_stream().synchronize()
+                        if io[3] != expect:
+                            raise RuntimeError(f"decode step {expect} did not publish its token")
+            self._seq = expect
+            return int(io[2])
         self._h_tok[0] = int(token)
         self.token.copy_(self._h_tok, non_blocking=True)
         self.step()

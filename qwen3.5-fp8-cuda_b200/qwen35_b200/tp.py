@@ -233,6 +233,7 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
         torch.cuda.synchronize(self.device)
         self.dist.barrier(group=self.group)
         self.graph = None
+        self.graph_io = None
         for pb in self._p2p_peers:
             self.lib.qwen_p2p_close(pb)
         self.lib.qwen_p2p_table_free(self._p2p_table)

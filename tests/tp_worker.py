@@ -10,9 +10,11 @@ single-GPU engine on the same weights:
   additions; a few BF16 roundings of the residual stream flip, and every
   following layer adds its own such flips (about 1e-3 per layer on the
   random-init 4B model);
-* over 10 greedy steps (CUDA graphs): the tokens are identical and the
-  logits gathered from the vocabulary shards agree within 5e-2 relative L2,
-  the drift of 32 layers of such flips.
+* over 10 greedy steps (CUDA graphs, both engines fed the single-GPU
+  engine's tokens): the logits gathered from the vocabulary shards agree
+  within 5e-2 relative L2, the drift of 32 layers of such flips, and the
+  tokens are identical except where the single-GPU top-2 logits are closer
+  than that drift (a near-tie).
 
 QWEN_TP_COLLECTIVE selects the exchange (p2p, the default, or nccl).
 """
@@ -75,33 +77,46 @@ def main():
         tp.reset()
         single.capture()
         tp.capture()
-        tok_s = tok_t = 101
+        # teacher forcing: both engines get the single-GPU engine's token, so
+        # one near-tie cannot make the sequences diverge
+        tok = 101
         errs, herrs = [], []
         nloc = tp.w["lm_head"][0].shape[0]
+        sizes = [torch.zeros(1, dtype=torch.int64, device="cuda") for _ in range(world)]
+        dist.all_gather(sizes, torch.tensor([nloc], device="cuda"))
+        sizes = [int(t.item()) for t in sizes]
+        nmax = max(sizes)
         for step in range(10):
-            tok_s = single.decode(tok_s)
-            tok_t = tp.decode(tok_t)
-            parts = [torch.empty(cfg.vocab_size // world, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
-            loc = tp.logits[:nloc].contiguous()
-            if nloc == cfg.vocab_size // world:
-                dist.all_gather(parts, loc)
-                lt = torch.cat(parts).float()
-                ls = single.logits.float()
-                errs.append(float((lt - ls).norm() / ls.norm()))
-                hs, ht = single.hidden.float(), tp.hidden.float()
-                herrs.append(float((ht - hs).norm() / hs.norm()))
+            tok_s = single.decode(tok)
+            tok_t = tp.decode(tok)
+            parts = [torch.empty(nmax, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+            loc = torch.zeros(nmax, dtype=torch.bfloat16, device="cuda")
+            loc[:nloc] = tp.logits[:nloc]
+            dist.all_gather(parts, loc)
+            lt = torch.cat([p_[:n] for p_, n in zip(parts, sizes)]).float()
+            ls = single.logits.float()
+            errs.append(float((lt - ls).norm() / ls.norm()))
+            hs, ht = single.hidden.float(), tp.hidden.float()
+            herrs.append(float((ht - hs).norm() / hs.norm()))
             if tok_s != tok_t:
-                ok = False
-                print(f"rank {rank} {name} step {step}: tokens differ {tok_s} vs {tok_t}", flush=True)
+                # accepted only at a near-tie: the single engine's top-2 logits
+                # closer than the drift of the gathered logits
+                top2 = torch.topk(ls, 2).values
+                gap = float(top2[0] - top2[1])
+                drift = float((lt - ls).abs().max())
+                print(f"rank {rank} {name} step {step}: tokens differ {tok_s} vs {tok_t}, "
+                      f"top-2 gap {gap:.3g}, max logit drift {drift:.3g}", flush=True)
+                if gap > drift:
+                    ok = False
+            tok = tok_s
         if not errs or max(errs) > 5e-2:
             ok = False
         if rank == 0:
             print(f"{name} ({collective}): logits rel_l2 per step " + " ".join(f"{e:.1e}" for e in errs), flush=True)
             print(f"{name}: final hidden rel_l2 per step " + " ".join(f"{e:.1e}" for e in herrs), flush=True)
         assert _lib.device_error() == 0
-        single.graph = None
+        single.graph = single.graph_io = None
         tp.close()
-        tp.graph = None
         del single, tp, w
         torch.cuda.empty_cache()
     flag = torch.tensor([1 if ok else 0], device="cuda")
