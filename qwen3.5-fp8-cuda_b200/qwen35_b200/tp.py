@@ -226,14 +226,16 @@ class Qwen35TPDecodeEngine(Qwen35DecodeEngine):
         dist.barrier(group=self.group)
 
     def close(self):
-        """Unmap the peers' exchange regions and free this rank's (collective:
-        every rank calls it, after its last step)."""
-        if self._p2p_base is None:
-            return
+        """Release the step graphs (with NCCL exchanges they hold NCCL calls,
+        which must go before the process group is destroyed), then unmap the
+        peers' exchange regions and free this rank's (collective: every rank
+        calls it, after its last step)."""
         torch.cuda.synchronize(self.device)
-        self.dist.barrier(group=self.group)
         self.graph = None
         self.graph_io = None
+        if self._p2p_base is None:
+            return
+        self.dist.barrier(group=self.group)
         for pb in self._p2p_peers:
             self.lib.qwen_p2p_close(pb)
         self.lib.qwen_p2p_table_free(self._p2p_table)
