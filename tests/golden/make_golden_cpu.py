@@ -20,11 +20,17 @@ Writes ``tests/golden/cpu_golden.safetensors``.  Cases:
 * ``conv_*``      HF torch_causal_conv1d_update as called at main.py:1097
 * ``delta_*``     HF torch_recurrent_gated_delta_rule on FP32 inputs
                   (use_qk_l2norm_in_kernel=True), the math of fused_kernels.cu:623-684
+* ``quant_*``     QwenEngineFP8Opt._quantize_bf16_to_fp8 (main.py:834-848) on a
+                  ragged 300 x 200 BF16 matrix with an all-zero block
+* ``load_*``      QwenEngineFP8Opt._load_weights_fp8 (main.py:573-720) on the
+                  micro checkpoint this script also writes to
+                  ``tests/golden/micro_ckpt/`` (config.json + model.safetensors)
 """
 
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import sys
 import types
@@ -63,6 +69,100 @@ def load_reference(ref_dir):
     import main as ref  # the reference engine module
     ref.DEV = "cpu"
     return ref
+
+
+MICRO = {  # a 2-layer member of the family, small enough to commit
+    "hidden_size": 128, "intermediate_size": 256, "num_hidden_layers": 2, "vocab_size": 320,
+    "num_attention_heads": 2, "num_key_value_heads": 1, "head_dim": 64,
+    "linear_num_key_heads": 1, "linear_num_value_heads": 2, "linear_key_head_dim": 64,
+    "linear_value_head_dim": 64, "linear_conv_kernel_dim": 4,
+    "layer_types": ["linear_attention", "full_attention"],
+    "rope_parameters": {"rope_theta": 10000000, "partial_rotary_factor": 0.25},
+}
+
+
+def make_micro_checkpoint(ckpt_dir, g):
+    """A block-FP8 checkpoint exercising every branch of the reference loader:
+    FP8 linears with FP32 scales that BF16 does not represent, an FP8 linear
+    without a scale tensor, a BF16 linear, norms stored BF16 and FP32, a BF16
+    dt_bias, conv1d as [C, 1, W], an FP8 LM head, and vision / MTP tensors the
+    decoder does not read."""
+    c = MICRO
+    H, I, V = c["hidden_size"], c["intermediate_size"], c["vocab_size"]
+    qd, kvd = c["num_attention_heads"] * c["head_dim"], c["num_key_value_heads"] * c["head_dim"]
+    nv, vd = c["linear_num_value_heads"], c["linear_num_value_heads"] * c["linear_value_head_dim"]
+    conv = 2 * c["linear_num_key_heads"] * c["linear_key_head_dim"] + vd
+    t = {}
+
+    def fp8(key, n, k, scaled=True):
+        t[key] = (torch.randn(n, k, generator=g) * 64).clamp(-448, 448).to(torch.float8_e4m3fn)
+        if scaled:
+            nb, kb = (n + 127) // 128, (k + 127) // 128
+            t[key + "_scale_inv"] = torch.pow(10.0, torch.rand(nb, kb, generator=g) * 2 - 4)
+
+    def vec(key, n, dtype, mean=0.0, std=0.02):
+        t[key] = (torch.randn(n, generator=g) * std + mean).to(dtype)
+
+    p = "model.language_model."
+    t[p + "embed_tokens.weight"] = (torch.randn(V, H, generator=g) * 0.02).to(BF16)
+    vec(p + "norm.weight", H, BF16)
+    fp8("lm_head.weight", V, H)
+    for i, lt in enumerate(c["layer_types"]):
+        b = f"{p}layers.{i}."
+        vec(b + "input_layernorm.weight", H, BF16)
+        vec(b + "post_attention_layernorm.weight", H, F32)
+        if lt == "linear_attention":
+            fp8(b + "linear_attn.in_proj_qkv.weight", conv, H)
+            t[b + "linear_attn.in_proj_a.weight"] = (torch.randn(nv, H, generator=g) * 0.05).to(BF16)
+            fp8(b + "linear_attn.in_proj_b.weight", nv, H, scaled=False)
+            fp8(b + "linear_attn.in_proj_z.weight", vd, H)
+            fp8(b + "linear_attn.out_proj.weight", H, vd)
+            t[b + "linear_attn.A_log"] = torch.log(torch.rand(nv, generator=g) * 15 + 1)
+            t[b + "linear_attn.dt_bias"] = (torch.rand(nv, generator=g) + 0.5).to(BF16)
+            t[b + "linear_attn.conv1d.weight"] = (torch.randn(conv, 1, 4, generator=g) * 0.1).to(BF16)
+            vec(b + "linear_attn.norm.weight", c["linear_value_head_dim"], F32, mean=1.0)
+        else:
+            fp8(b + "self_attn.q_proj.weight", 2 * qd, H)
+            fp8(b + "self_attn.k_proj.weight", kvd, H)
+            fp8(b + "self_attn.v_proj.weight", kvd, H)
+            fp8(b + "self_attn.o_proj.weight", H, qd)
+            vec(b + "self_attn.q_norm.weight", c["head_dim"], BF16)
+            vec(b + "self_attn.k_norm.weight", c["head_dim"], F32)
+        fp8(b + "mlp.gate_proj.weight", I, H)
+        fp8(b + "mlp.up_proj.weight", I, H)
+        fp8(b + "mlp.down_proj.weight", H, I)
+    t["model.visual.patch_embed.proj.weight"] = torch.randn(8, 8, generator=g).to(BF16)
+    t["mtp.fc.weight"] = torch.randn(8, 8, generator=g).to(BF16)
+    os.makedirs(ckpt_dir, exist_ok=True)
+    with open(os.path.join(ckpt_dir, "config.json"), "w") as f:
+        json.dump({"text_config": MICRO, "tie_word_embeddings": False}, f, indent=1)
+    save_file({k: v.contiguous() for k, v in t.items()}, os.path.join(ckpt_dir, "model.safetensors"),
+              metadata={"format": "pt"})
+
+
+def load_with_reference(Eng, ckpt_dir):
+    """QwenEngineFP8Opt._load_weights_fp8 (main.py:573-720) run on a stub with
+    the attributes it reads; its closing CUDA synchronize and memory report
+    are replaced by no-ops (no GPU here).  Returns its tensors, flattened."""
+    with open(os.path.join(ckpt_dir, "config.json")) as f:
+        tc = json.load(f)["text_config"]
+    stub = types.SimpleNamespace(n_layers=tc["num_hidden_layers"], layer_types=tc["layer_types"],
+                                 _quantize_bf16_to_fp8=Eng._quantize_bf16_to_fp8)
+    sync, mem = torch.cuda.synchronize, torch.cuda.memory_allocated
+    torch.cuda.synchronize, torch.cuda.memory_allocated = (lambda *a, **k: None), (lambda *a, **k: 0)
+    try:
+        Eng._load_weights_fp8(stub, ckpt_dir)
+    finally:
+        torch.cuda.synchronize, torch.cuda.memory_allocated = sync, mem
+    res = {"embed": stub.embed, "norm_f": stub.norm_f,
+           "lm_head_w": stub.lm_head_fp8, "lm_head_s": stub.lm_head_scale}
+    for i, ly in enumerate(stub.layers):
+        for name, v in ly.items():
+            if isinstance(v, tuple):
+                res[f"L{i}_{name}_w"], res[f"L{i}_{name}_s"] = v
+            elif isinstance(v, torch.Tensor):
+                res[f"L{i}_{name}"] = v
+    return res
 
 
 def main():
@@ -177,6 +277,18 @@ def main():
     for name, t in {"q": q, "k": k, "v": v, "g": gg, "beta": bb, "state_in": s0, "out": o,
                     "state_out": s1}.items():
         out[f"delta_{name}"] = t.contiguous()
+
+    # ---- checkpoint loading and BF16 -> block-FP8 quantization ----
+    # own generator: the cases above keep their random streams
+    gq = torch.Generator().manual_seed(4321)
+    wq_in = (torch.randn(300, 200, generator=gq) * torch.rand(300, 1, generator=gq) * 4).to(BF16)
+    wq_in[128:256, 0:128] = 0  # an all-zero block: the scale's 1e-12 floor
+    qw, qs = Eng._quantize_bf16_to_fp8(wq_in)
+    out["quant_w_in"], out["quant_w"], out["quant_s"] = wq_in, qw.view(torch.uint8), qs
+    ckpt_dir = os.path.join(HERE, "micro_ckpt")
+    make_micro_checkpoint(ckpt_dir, gq)
+    for k_, v_ in load_with_reference(Eng, ckpt_dir).items():
+        out["load_" + k_] = v_
 
     out = {k_: v_.contiguous() for k_, v_ in out.items()}
     save_file(out, args.out)

@@ -88,3 +88,22 @@ def test_full_size_engine_runs_and_is_deterministic():
     assert out1 == out2
     assert all(0 <= t < cfg.vocab_size for t in out1)
     assert _lib.device_error() == 0
+
+
+def test_engine_from_saved_checkpoint(tmp_path):
+    """save_checkpoint -> load_checkpoint(device="cuda") feeds the engine the
+    same bits: greedy tokens and logits equal those of the in-memory weights."""
+    from qwen35_b200.checkpoint import load_checkpoint, save_checkpoint
+    cfg, w_cpu, eng_a = make_tiny(seed=2)
+    save_checkpoint(w_cpu, cfg, str(tmp_path), max_shard_bytes=1 << 20)
+    w_dev = load_checkpoint(str(tmp_path), device="cuda")
+    assert w_dev["lm_head"][0].is_cuda and w_dev["layers"][0]["in_proj_qkv"][1].is_cuda
+    from qwen35_b200.engine import Qwen35DecodeEngine
+    eng_b = Qwen35DecodeEngine(cfg, w_dev, max_seq=eng_a.max_seq, keep_logits=True)
+    eng_a.capture()
+    eng_b.capture()
+    t_a = t_b = 7
+    for _ in range(10):
+        t_a, t_b = eng_a.decode(t_a), eng_b.decode(t_b)
+        assert t_a == t_b
+        assert torch.equal(eng_a.logits, eng_b.logits)
