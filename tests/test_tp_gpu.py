@@ -1,4 +1,4 @@
-"""Tensor-parallel decode on 2 GPUs of one box (skipped with fewer GPUs).
+"""Tensor-parallel decode on 2 and 4 GPUs of one box (each skipped with fewer GPUs).
 
 Runs tests/tp_worker.py under torch.distributed.run, with the exchanges over
 NVLink peer memory (p2p) and through NCCL: greedy tokens must equal the
@@ -15,13 +15,15 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("collective,port", [("p2p", 29531), ("nccl", 29533)])
-def test_tp2_matches_single_gpu(collective, port):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world,collective,port", [(2, "p2p", 29531), (2, "nccl", 29533), (4, "p2p", 29535)],
+                         ids=["tp2-p2p", "tp2-nccl", "tp4-p2p"])
+def test_tp_matches_single_gpu(world, collective, port):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     here = os.path.dirname(os.path.abspath(__file__))
     cmd = ["timeout", "-k", "60", "800", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}", os.path.join(here, "tp_worker.py")]
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}",
+           os.path.join(here, "tp_worker.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", QWEN_TP_COLLECTIVE=collective)
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
     print(r.stdout[-3000:], r.stderr[-3000:])
