@@ -1,11 +1,11 @@
 """Generate CPU golden fixtures by running the reference's own Python code.
 
-Run in a container that has the reference checkout (default /root/reference)
+Run in a container that has the reference checkout (the --ref argument)
 and the reference kernels built by ``oracle/Makefile`` (``oracle/_ref``); the
 reference's ``main.py`` opens those libraries at import time but nothing here
 launches a GPU kernel: every call below is a CPU torch path of the reference.
 
-    python tests/golden/make_golden_cpu.py [--ref /root/reference]
+    python tests/golden/make_golden_cpu.py [--ref REFERENCE_CHECKOUT]
 
 Writes ``tests/golden/cpu_golden.safetensors``.  Cases:
 
