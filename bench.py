@@ -13,12 +13,15 @@ than the 126 MB L2, so no flush is needed between steps.
 
 Keys beyond the base contract:
   e2e           the same K steps through the public API Qwen35DecodeEngine.decode()
-                (token H2D from pinned memory + graph + token D2H + sync per step)
+                (token in from pinned memory, graph replay, next token and a
+                sequence number written to pinned memory, host polls)
   roofline      the dominant kernel (gemv_tcw_kernel, the tcgen05 + TMA GEMV with
                 the weights as the N = 256 MMA operand and the fused greedy
                 argmax) timed alone on the LM-head launch of config 2, back to
                 back (burst peak)
   step_roofline algorithmic bytes of a whole decode step / device time per step
+  gemv_shapes   (1 GPU) every config 0/1 decode GEMV shape timed alone, through the
+                reference entry point and PDL-chained (qwen35_b200.profile_gemv)
   cpu_baseline  the CPU oracle port (explicit FP8->FP32 dequant + torch matmul)
                 on a bounded sample of the step, scaled to tok/s
   clocks        nvidia-smi samples taken during the timed region
@@ -475,6 +478,14 @@ def run_ours(args):
         "clocks": clocks,
         "pdl": not args.no_pdl,
     }
+    if world == 1:
+        # every config 0/1 decode GEMV shape alone (after the timed region)
+        from qwen35_b200.profile_gemv import time_shapes
+        line["gemv_shapes"] = {
+            "unit": "us per launch; GB/s of algorithmic bytes; frac of the measured peak",
+            "method": "CUDA graph of back-to-back launches over rotating weight copies; abi = "
+                      "launch_gemv_v4_extern (no PDL), chained = qwen_linear_partial (PDL)",
+            "rows": time_shapes(peak)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = run_cpu_baseline(cfg)

@@ -153,6 +153,16 @@ int qwen_set_gated_input(const void* z, const void* norm_w, float eps);
 /* y = bf16(res + bf16(W x)): o_proj / out_proj / down with the residual add (553-559). */
 int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K, int K_blk, const void* res, void* y,
                       cudaStream_t stream);
+/* Replaces the residual-add launch pair of the same projections (553-559) on
+ * one GPU: W x as per-K-slice FP32 partial rows slices[c][r], c < *count
+ * (count <= max_slices, written by the launch), with no reduction of its own.
+ * The next RMSNorm-prologue launch on this host thread, after
+ * qwen_set_slices_input(slices, count, n, max_slices, res), builds its input
+ * as bf16(res + bf16(sum of the slices in order)), writes it to the buffer
+ * passed as its x (the residual stream) and normalises it. */
+int qwen_linear_slices(const void* x, const void* w, const void* s, int N, int K, int K_blk, float* slices,
+                       int* count, int max_slices, cudaStream_t stream);
+int qwen_set_slices_input(const float* slices, const int* count, int n, int max_slices, const void* res);
 /* Tensor parallelism (row/column sharding of the decode step across GPUs;
  * the reference has no multi-GPU path, these replace nothing):
  * y_f32 = this rank's partial GEMV over its slice of K, to be all-reduced. */

@@ -26,6 +26,7 @@ enum : unsigned {
   ERR_TIMEOUT_EMPTY = 2,    // producer gave up waiting for a free stage
   ERR_TIMEOUT_DRAIN = 3,    // producer gave up waiting for its own copies
   ERR_POS_RANGE = 5,        // a device-side cache position outside [0, max_seq)
+  ERR_SLICES_COUNT = 7,     // a K-slice count outside [1, sl_max] (PRO_SLICES_RMSNORM)
 };
 
 // One error word per shared library (each library is a single translation

@@ -61,6 +61,8 @@ enum GemvEpi : int {
   EPI_GATE_BETA = 6,  // y[r] = bf16(sigmoid(bf16(v)))
   EPI_F32 = 7,        // y(f32)[r] = v (partial sums of a K-sliced tensor-parallel GEMV)
   EPI_F32_P2P = 8,    // v into slot [rank] of every rank's exchange buffer (aux0 = P2PTable*)
+  EPI_SLICES = 9,     // y(f32)[slice * n + r] = this K slice's partial v; y2 (int*) = slice count
+                      // (tensor-core kernel, one segment: the next launch adds the slices)
 };
 
 enum GemvPro : int {
@@ -69,6 +71,8 @@ enum GemvPro : int {
   PRO_ADD_RMSNORM = 2,  // h2 <- bf16(x + x2) (stored by CTA 0); x <- rmsnorm(h2)
   PRO_P2P_RMSNORM = 3,  // h2 <- bf16(x + bf16(sum of the ranks' partials, p2p)) (stored by CTA 0); x <- rmsnorm(h2)
   PRO_GATED_NORM = 4,   // per 128-block (one GatedDeltaNet head): x <- RMSNormGated(x, z) (gz, gw, eps)
+  PRO_SLICES_RMSNORM = 5,  // h2 <- bf16(x + bf16(sum of the previous launch's EPI_SLICES rows in slice
+                           // order)) (stored by CTA 0); x <- rmsnorm(h2)
 };
 
 struct GemvSeg {
@@ -112,6 +116,10 @@ struct GemvArgs {
   const P2PTable* p2p;             // PRO_P2P_RMSNORM: the tensor-parallel exchange of this round
   const bf16* gz;                  // PRO_GATED_NORM: gate z, same layout as x
   const bf16* gw;                  // PRO_GATED_NORM: norm weight of one 128-wide head
+  const float* sl_buf;             // PRO_SLICES_RMSNORM: the slices [count][sl_n]
+  const int* sl_count;             // PRO_SLICES_RMSNORM: their count (written by the producing launch)
+  int sl_n;                        // PRO_SLICES_RMSNORM: row stride of sl_buf (== K)
+  int sl_max;                      // EPI_SLICES / PRO_SLICES_RMSNORM: slices the buffer holds
   GemvSeg seg[GEMV_MAX_SEG];
 };
 
@@ -213,6 +221,7 @@ __device__ __noinline__ unsigned long long gemv_epilogue(const GemvSeg& sg, int 
       reinterpret_cast<bf16*>(sg.y)[r] = f2bf(1.0f / (1.0f + expf(-b)));
     } break;
     case EPI_F32:
+    case EPI_SLICES:  // slice 0 of an unsplit launch
       reinterpret_cast<float*>(sg.y)[r] = v;
       break;
     case EPI_F32_P2P:

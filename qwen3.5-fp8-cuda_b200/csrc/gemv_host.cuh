@@ -243,9 +243,12 @@ static cudaError_t gemv_tc_run(GemvArgs a, bool f32_scales, cudaStream_t st, boo
   int best_c = 0;
   double best_cost = 0;
   const int cmin = (nkb + 31) / 32;
-  for (int c = cmin; c <= nkb && c <= 64 && c <= sms; ++c) {
+  // EPI_SLICES: at most sl_max slices (the rows the caller's buffer holds)
+  const int cmax = a.seg[0].epi == EPI_SLICES ? a.sl_max : 64;
+  for (int c = cmin; c <= nkb && c <= cmax && c <= sms; ++c) {
     const long long items = (long long)nunits * c;
-    if (c > 1 && (items * P * TC_ROWS > TC_PART_FLOATS || nunits > TC_MAX_CNT)) break;
+    if (c > 1 && a.seg[0].epi != EPI_SLICES && (items * P * TC_ROWS > TC_PART_FLOATS || nunits > TC_MAX_CNT))
+      break;
     const long long slots = (long long)(sms / c) * c;
     const long long waves = (items + slots - 1) / slots;
     const double cost = (double)waves * ((nkb + c - 1) / c + 2) + (c > 1 ? 1.0 + c / 8.0 : 0.0);
@@ -387,6 +390,7 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
     if (sg.n < 0 || !sg.w || !sg.s) return cudaErrorInvalidValue;
     if (sg.epi != EPI_ARGMAX && sg.epi != EPI_F32_P2P && sg.n > 0 && !sg.y) return cudaErrorInvalidValue;
     if (sg.epi == EPI_F32_P2P && !sg.aux0) return cudaErrorInvalidValue;
+    if (sg.epi == EPI_SLICES && (!sg.y2 || a.nseg != 1 || a.sl_max < 1)) return cudaErrorInvalidValue;
     if (sg.epi == EPI_SILU_PAIR && (!sg.w2 || !sg.s2)) return cudaErrorInvalidValue;
     if (sg.epi == EPI_CONV && (sg.cw < 1 || sg.cw > 8 || !sg.aux0 || !sg.aux2)) return cudaErrorInvalidValue;
     if (sg.epi == EPI_ARGMAX && !a.am_ws) return cudaErrorInvalidValue;
@@ -410,10 +414,13 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
       }
       wide = pair || bytes >= tcw_min_bytes();
     }
+    if (a.seg[0].epi == EPI_SLICES) wide = false;  // the M = 128 kernel writes slices
     const cudaError_t e = wide ? gemv_tcw_run(a, f32_scales, st, pdl) : gemv_tc_run(a, f32_scales, st, pdl);
     if (e != cudaErrorNotSupported) return e;
   }
-  if (a.pro == PRO_P2P_RMSNORM || a.pro == PRO_GATED_NORM) return cudaErrorNotSupported;  // tcgen05 kernels only
+  if (a.pro == PRO_P2P_RMSNORM || a.pro == PRO_GATED_NORM || a.pro == PRO_SLICES_RMSNORM ||
+      a.seg[0].epi == EPI_SLICES)
+    return cudaErrorNotSupported;  // tcgen05 kernels only
   if (npair != 0 && npair != a.nseg) mma_ok = false;
   if (mma_ok && (a.K / 128 + GEMV_WARPS - 1) / GEMV_WARPS > 32) mma_ok = false;  // K > 32768
   if (mma_ok) {

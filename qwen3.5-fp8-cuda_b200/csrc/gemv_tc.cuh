@@ -203,14 +203,27 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
     pn = pt.n;
     named_bar(1, NT);
   }
+  // Single-GPU input: the previous launch's K-slice partial rows (EPI_SLICES,
+  // complete once griddepcontrol.wait has returned).  A count outside
+  // [1, sl_max] is recorded as an error and read as no slices.
+  if (a.pro == PRO_SLICES_RMSNORM) {
+    pbuf = a.sl_buf;
+    pworld = *reinterpret_cast<const volatile int*>(a.sl_count);
+    pn = a.sl_n;
+    if (pworld < 1 || pworld > a.sl_max) {
+      if (t == 0 && blockIdx.x == 0) qwen_err_set(ERR_SLICES_COUNT);
+      pworld = 0;
+    }
+  }
+  const bool psum = a.pro == PRO_P2P_RMSNORM || a.pro == PRO_SLICES_RMSNORM;
   // pass 1: up to MAXC chunks of 8 elements per thread are loaded before any
   // is used, so the loads overlap
   float ss = 0.f;
   const int nch = K >> 3;
-  // Tensor-parallel input: h = bf16(res + bf16(sum of the ranks' partials in
-  // rank order)), two chunks per thread in flight, the ranks' loads of both
-  // chunks issued before they are added.
-  for (int base = t; a.pro == PRO_P2P_RMSNORM && base < nch; base += NT * 2) {
+  // Tensor-parallel or sliced input: h = bf16(res + bf16(sum of the ranks' (or
+  // slices') partials in order)), two chunks per thread in flight, the loads
+  // of one rank (slice) for both chunks issued before they are added.
+  for (int base = t; psum && base < nch; base += NT * 2) {
     uint4 v[2];
     float sum[2][8];
 #pragma unroll
@@ -254,7 +267,7 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
       if (b >= kb0 && b < kb0 + nxb) reinterpret_cast<uint4*>(stg)[i - kb0 * 16] = v[j];
     }
   }
-  for (int base = t; a.pro != PRO_P2P_RMSNORM && base < nch; base += NT * MAXC) {
+  for (int base = t; !psum && base < nch; base += NT * MAXC) {
     uint4 v[MAXC], r[MAXC];
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
@@ -611,6 +624,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int row = t.row0 + r;
         if (C == 1) {
           if (row < sg.n) am_best = gemv_epilogue(sg, row, acc[0], PAIR ? acc[P - 1] : 0.f, am_best);
+        } else if (sg.epi == EPI_SLICES) {
+          // K split without the reduction: the next launch adds the slices
+          if (row < sg.n) reinterpret_cast<float*>(sg.y)[(size_t)csl * sg.n + row] = acc[0];
         } else {
           // K split: publish this slice, the last CTA of the unit reduces in slice order
           float* part = g_tc_part + (size_t)i * P * TC_ROWS;
@@ -654,6 +670,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   if (a.am_ws) argmax_finish(a, am_best, am_misc);
   if (a.pro == PRO_P2P_RMSNORM && threadIdx.x == 0) p2p_round_done(*a.p2p);
+  if (a.seg[0].epi == EPI_SLICES && blockIdx.x == 0 && threadIdx.x == 0) *static_cast<int*>(a.seg[0].y2) = C;
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(TC_TMEM_COLS) : "memory");

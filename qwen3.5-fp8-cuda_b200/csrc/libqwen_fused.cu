@@ -60,8 +60,44 @@ inline cudaError_t take_gated_input(GemvArgs& a) {
   return cudaSuccess;
 }
 
+// Single-GPU sliced input of the next RMSNorm-prologue launch on this host
+// thread (set by qwen_set_slices_input, consumed and cleared by that launch):
+// the launch builds its x as bf16(res + bf16(sum of the previous launch's
+// K-slice rows)), writes it to the buffer it was given as x, and normalises it.
+thread_local const float* g_sl_buf = nullptr;
+thread_local const int* g_sl_count = nullptr;
+thread_local const void* g_sl_res = nullptr;
+thread_local int g_sl_n = 0;
+thread_local int g_sl_max = 0;
+
+inline cudaError_t take_slices_input(GemvArgs& a) {
+  if (!g_sl_buf) return cudaSuccess;
+  const float* b = g_sl_buf;
+  const int* c = g_sl_count;
+  const void* r = g_sl_res;
+  const int n = g_sl_n, mx = g_sl_max;
+  g_sl_buf = nullptr;
+  g_sl_count = nullptr;
+  g_sl_res = nullptr;
+  g_sl_n = g_sl_max = 0;
+  if (a.pro != PRO_RMSNORM || n != a.K || a.xn_out || a.h2_out || a.x_row) return cudaErrorInvalidValue;
+  a.pro = PRO_SLICES_RMSNORM;
+  a.sl_buf = b;
+  a.sl_count = c;
+  a.sl_n = n;
+  a.sl_max = mx;
+  a.h2_out = const_cast<bf16*>(a.x);
+  a.x = static_cast<const bf16*>(r);
+  return cudaSuccess;
+}
+
 inline cudaError_t take_p2p_input(GemvArgs& a) {
-  if (!g_p2p_table) return cudaSuccess;
+  if (g_sl_buf && g_p2p_table) {  // one pending input at a time: drop both
+    g_sl_buf = nullptr;
+    g_p2p_table = nullptr;
+    return cudaErrorInvalidValue;
+  }
+  if (!g_p2p_table) return take_slices_input(a);
   const void* t = g_p2p_table;
   const void* r = g_p2p_res;
   const int n = g_p2p_n;
@@ -175,6 +211,16 @@ int qwen_set_gated_input(const void* z, const void* norm_w, float eps) {
   g_gz = z;
   g_gw = norm_w;
   g_geps = eps;
+  return 0;
+}
+
+int qwen_set_slices_input(const float* slices, const int* count, int n, int max_slices, const void* res) {
+  if (!slices || !count || !res || n <= 0 || max_slices < 1) return record(cudaErrorInvalidValue);
+  g_sl_buf = slices;
+  g_sl_count = count;
+  g_sl_res = res;
+  g_sl_n = n;
+  g_sl_max = max_slices;
   return 0;
 }
 
@@ -583,6 +629,23 @@ int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K,
   a.nseg = 1;
   a.seg[0] = seg(w, s, y, N, K_blk, EPI_RESID);
   a.seg[0].aux0 = res;
+  a.pf = take_prefetch();
+  if (cudaError_t ge = take_gated_input(a)) return record(ge);
+  return record(gemv_run(a, false, stream, engine_pdl()));
+}
+
+// y = W x as per-K-slice FP32 partial rows: slices[c][r] for c < *count
+// (count <= max_slices, written by the launch).  The next RMSNorm-prologue
+// launch, given qwen_set_slices_input, adds them (in slice order) to its
+// residual; nothing reduces them here.
+int qwen_linear_slices(const void* x, const void* w, const void* s, int N, int K, int K_blk, float* slices,
+                       int* count, int max_slices, cudaStream_t stream) {
+  if (!slices || !count || max_slices < 1) return record(cudaErrorInvalidValue);
+  GemvArgs a = make_args(x, K);
+  a.nseg = 1;
+  a.seg[0] = seg(w, s, slices, N, K_blk, EPI_SLICES);
+  a.seg[0].y2 = count;
+  a.sl_max = max_slices;
   a.pf = take_prefetch();
   if (cudaError_t ge = take_gated_input(a)) return record(ge);
   return record(gemv_run(a, false, stream, engine_pdl()));

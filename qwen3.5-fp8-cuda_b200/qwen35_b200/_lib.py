@@ -62,6 +62,8 @@ NEW_FUSED = {
     "qwen_gdn_in_proj": (I, [P, P, F, I, I, P, P, I, P, P, I, P, P, P, I, P, P, P, P, P, I, P, P, P, P, P]),
     "qwen_gdn_decode": (I, [P, P, P, P, P, P, F, P, I, I, I, P]),
     "qwen_linear_resid": (I, [P, P, P, I, I, I, P, P, P]),
+    "qwen_linear_slices": (I, [P, P, P, I, I, I, P, P, I, P]),
+    "qwen_set_slices_input": (I, [P, P, I, I, P]),
     "qwen_mlp_gate_up": (I, [P, P, F, P, P, P, P, I, I, I, P, P]),
     "qwen_attn_decode": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, I, I, P, P, P, P]),
     "qwen_attn_decode_noalloc": (I, [P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, F, I, I, P, P]),

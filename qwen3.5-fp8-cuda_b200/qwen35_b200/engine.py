@@ -60,11 +60,21 @@ class Qwen35DecodeEngine:
     (``cp.async.bulk.prefetch``) while it runs.  It is off by default: on B200
     the prefetches compete with the running launch's own stream and the step
     measured about 8% slower with them.
+
+    ``slices`` (default on): o_proj, out_proj and down write their K-split
+    partial rows (``qwen_linear_slices``) instead of reducing them in a last
+    CTA and adding the residual; the next launch (gate/up, the next layer's
+    in_proj, the LM head) adds the slices in slice order to the residual in
+    its prologue and writes the new residual stream.  Same arithmetic, one
+    store / fence / atomic / reload chain less per projection.  ``hidden``
+    holds the residual stream only once the launch after a layer has run.
     """
 
     def __init__(self, cfg, weights, max_seq: int = 4096, device="cuda", keep_logits: bool = False,
-                 attn_chunk: int | None = None, prefetch: bool = False, gdn_split: bool = False):
+                 attn_chunk: int | None = None, prefetch: bool = False, gdn_split: bool = False,
+                 slices: bool = True):
         self.cfg = cfg
+        self.slices = bool(slices)
         self.gdn_split = bool(gdn_split) and cfg.linear_value_head_dim == 128
         self.prefetch = prefetch
         self.w = weights
@@ -81,6 +91,11 @@ class Qwen35DecodeEngine:
 
         self.hidden = empty(H)
         self.h2 = empty(H)
+        # K-slice partial rows of the residual projections (o_proj / out_proj /
+        # down) and their count, summed by the next launch's prologue
+        self.sl_max = 16
+        self.sl_buf = empty(self.sl_max * H, f32)
+        self.sl_count = torch.zeros(1, dtype=torch.int32, device=dev)
         qd = cfg.num_attention_heads * cfg.head_dim
         kvd = cfg.num_key_value_heads * cfg.head_dim
         self.q_all = empty(2 * qd)
@@ -164,35 +179,57 @@ class Qwen35DecodeEngine:
         def chk(status, what):
             _lib.check(status, what)
 
+        def resid(st, x, wt, scl, res, out, what):
+            """out = res + W x: one launch, or (slices) the K-slice rows that the
+            next launch adds to res (it writes out)."""
+            if self.slices:
+                chk(lib.qwen_linear_slices(_p(x), _p(wt), _p(scl), wt.shape[0], wt.shape[1],
+                                           scale_mode(wt.shape[0], scl), _p(self.sl_buf), _p(self.sl_count),
+                                           self.sl_max, st), what)
+            else:
+                chk(lib.qwen_linear_resid(_p(x), _p(wt), _p(scl), wt.shape[0], wt.shape[1],
+                                          scale_mode(wt.shape[0], scl), _p(res), _p(out), st), what)
+
+        def take(res):
+            """The next launch builds its input from the pending slices plus res."""
+            if self.slices:
+                chk(lib.qwen_set_slices_input(_p(self.sl_buf), _p(self.sl_count), H, self.sl_max, _p(res)),
+                    "slices_input")
+
         plan.append((lambda st: chk(lib.qwen_embed(_p(w["embed"]), _p(self.token), _p(self.hidden), H, st),
                                     "qwen_embed"), []))
         for i, ly in enumerate(w["layers"]):
             if cfg.layer_types[i] == "full_attention":
                 (wq, sq), (wk, sk), (wv, sv), (wo, so) = ly["q_proj"], ly["k_proj"], ly["v_proj"], ly["o_proj"]
-                plan.append((lambda st, ly=ly, wq=wq, sq=sq, wk=wk, sk=sk, wv=wv, sv=sv: chk(lib.qwen_attn_in_proj(
-                    _p(self.hidden), _p(ly["input_layernorm"]), eps, _p(wq), _p(sq), wq.shape[0], _p(wk), _p(sk),
-                    wk.shape[0], _p(wv), _p(sv), wv.shape[0], H, scale_mode(wq.shape[0], sq), _p(self.q_all),
-                    _p(self.k_new), _p(self.v_new), st), "attn_in_proj"), self._regions(wq, wk, wv)))
+                def attn_in(st, i=i, ly=ly, wq=wq, sq=sq, wk=wk, sk=sk, wv=wv, sv=sv):
+                    if i > 0:
+                        take(self.h2)
+                    chk(lib.qwen_attn_in_proj(
+                        _p(self.hidden), _p(ly["input_layernorm"]), eps, _p(wq), _p(sq), wq.shape[0], _p(wk),
+                        _p(sk), wk.shape[0], _p(wv), _p(sv), wv.shape[0], H, scale_mode(wq.shape[0], sq),
+                        _p(self.q_all), _p(self.k_new), _p(self.v_new), st), "attn_in_proj")
+                plan.append((attn_in, self._regions(wq, wk, wv)))
                 plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_attn_decode(
                     _p(self.q_all), _p(self.k_new), _p(self.v_new), _p(ly["q_norm"]), _p(ly["k_norm"]),
                     _p(self.cos), _p(self.sin), _p(self.k_cache[i]), _p(self.v_cache[i]), _p(self.pos),
                     self.max_seq, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim, cfg.rotary_dim, eps,
                     self.attn_chunk, self.attn_nsplit, _p(self.attn_ws), _p(self.attn_cnt), _p(self.attn_out), st),
                     "attn_decode"), []))  # a decode step reads pos + 1 cache rows, not the whole cache
-                plan.append((lambda st, wo=wo, so=so: chk(lib.qwen_linear_resid(
-                    _p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
-                    _p(self.hidden), _p(self.h2), st), "o_proj"), self._regions(wo)))
+                plan.append((lambda st, wo=wo, so=so: resid(st, self.attn_out, wo, so, self.hidden, self.h2, "o_proj"),
+                             self._regions(wo)))
             else:
                 (wqkv, sqkv), (wz, sz) = ly["in_proj_qkv"], ly["in_proj_z"]
                 (wa, sa), (wb, sb), (wo, so) = ly["in_proj_a"], ly["in_proj_b"], ly["out_proj"]
-                plan.append((lambda st, ly=ly, i=i, wqkv=wqkv, sqkv=sqkv, wz=wz, sz=sz, wa=wa, sa=sa, wb=wb, sb=sb:
-                             chk(lib.qwen_gdn_in_proj(
-                                 _p(self.hidden), _p(ly["input_layernorm"]), eps, H, scale_mode(wqkv.shape[0], sqkv),
-                                 _p(wqkv), _p(sqkv), wqkv.shape[0], _p(ly["conv1d_w"]), _p(self.conv_state[i]),
-                                 cfg.linear_conv_kernel_dim, _p(self.qkv_conv), _p(wz), _p(sz), wz.shape[0],
-                                 _p(self.z), _p(wa), _p(sa), _p(wb), _p(sb), wa.shape[0], _p(ly["A_log"]),
-                                 _p(ly["dt_bias"]), _p(self.g), _p(self.beta), st), "gdn_in_proj"),
-                             self._regions(wqkv, wz, wa, wb)))
+                def gdn_in(st, ly=ly, i=i, wqkv=wqkv, sqkv=sqkv, wz=wz, sz=sz, wa=wa, sa=sa, wb=wb, sb=sb):
+                    if i > 0:
+                        take(self.h2)
+                    chk(lib.qwen_gdn_in_proj(
+                        _p(self.hidden), _p(ly["input_layernorm"]), eps, H, scale_mode(wqkv.shape[0], sqkv),
+                        _p(wqkv), _p(sqkv), wqkv.shape[0], _p(ly["conv1d_w"]), _p(self.conv_state[i]),
+                        cfg.linear_conv_kernel_dim, _p(self.qkv_conv), _p(wz), _p(sz), wz.shape[0],
+                        _p(self.z), _p(wa), _p(sa), _p(wb), _p(sb), wa.shape[0], _p(ly["A_log"]),
+                        _p(ly["dt_bias"]), _p(self.g), _p(self.beta), st), "gdn_in_proj")
+                plan.append((gdn_in, self._regions(wqkv, wz, wa, wb)))
                 if self.gdn_split:
                     # recurrent step over 4 CTAs per head; the gated norm runs in
                     # out_proj's prologue (one 128-wide K-block per head)
@@ -203,9 +240,7 @@ class Qwen35DecodeEngine:
 
                     def out_proj(st, ly=ly, wo=wo, so=so):
                         chk(lib.qwen_set_gated_input(_p(self.z), _p(ly["norm_w"]), eps), "gated_input")
-                        chk(lib.qwen_linear_resid(
-                            _p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
-                            _p(self.hidden), _p(self.h2), st), "out_proj")
+                        resid(st, self.attn_out, wo, so, self.hidden, self.h2, "out_proj")
                     plan.append((out_proj, self._regions(wo)))
                 else:
                     plan.append((lambda st, ly=ly, i=i: chk(lib.qwen_gdn_decode(
@@ -213,24 +248,27 @@ class Qwen35DecodeEngine:
                         _p(ly["norm_w"]), eps, _p(self.attn_out), cfg.linear_num_key_heads,
                         cfg.linear_num_value_heads, cfg.linear_value_head_dim, st), "gdn_decode"),
                         self._regions(self.state[i])))
-                    plan.append((lambda st, wo=wo, so=so: chk(lib.qwen_linear_resid(
-                        _p(self.attn_out), _p(wo), _p(so), wo.shape[0], wo.shape[1], scale_mode(wo.shape[0], so),
-                        _p(self.hidden), _p(self.h2), st), "out_proj"), self._regions(wo)))
+                    plan.append((lambda st, wo=wo, so=so: resid(st, self.attn_out, wo, so, self.hidden, self.h2,
+                                                                 "out_proj"), self._regions(wo)))
             (wg, sg), (wu, su), (wd, sd) = ly["gate_proj"], ly["up_proj"], ly["down_proj"]
-            plan.append((lambda st, ly=ly, wg=wg, sg=sg, wu=wu, su=su: chk(lib.qwen_mlp_gate_up(
-                _p(self.h2), _p(ly["post_attention_layernorm"]), eps, _p(wg), _p(sg), _p(wu), _p(su), I, H,
-                scale_mode(I, sg), _p(self.silu), st), "gate_up"), self._regions(wg, wu)))
-            plan.append((lambda st, wd=wd, sd=sd: chk(lib.qwen_linear_resid(
-                _p(self.silu), _p(wd), _p(sd), H, I, scale_mode(H, sd), _p(self.h2), _p(self.hidden), st), "down"),
-                self._regions(wd)))
+            def gate_up(st, ly=ly, wg=wg, sg=sg, wu=wu, su=su):
+                take(self.hidden)
+                chk(lib.qwen_mlp_gate_up(
+                    _p(self.h2), _p(ly["post_attention_layernorm"]), eps, _p(wg), _p(sg), _p(wu), _p(su), I, H,
+                    scale_mode(I, sg), _p(self.silu), st), "gate_up")
+            plan.append((gate_up, self._regions(wg, wu)))
+            plan.append((lambda st, wd=wd, sd=sd: resid(st, self.silu, wd, sd, self.h2, self.hidden, "down"),
+                         self._regions(wd)))
         head = w["lm_head"]
         if not isinstance(head, tuple):
             raise NotImplementedError("BF16 LM head: use an FP8 head (cfg.fp8_lm_head=True)")
         wh, sh = head
-        plan.append((lambda st: chk(lib.launch_lm_head_argmax(
-            _p(self.hidden), _p(w["norm_f"]), eps, _p(wh), _p(sh), wh.shape[0], H, scale_mode(wh.shape[0], sh), 0,
-            _p(self.am_ws), _p(self.key), _p(self.token), _p(self.logits), _p(self.pos), st), "lm_head_argmax"),
-            self._regions(wh)))
+        def lm_head(st):
+            take(self.h2)
+            chk(lib.launch_lm_head_argmax(
+                _p(self.hidden), _p(w["norm_f"]), eps, _p(wh), _p(sh), wh.shape[0], H, scale_mode(wh.shape[0], sh), 0,
+                _p(self.am_ws), _p(self.key), _p(self.token), _p(self.logits), _p(self.pos), st), "lm_head_argmax")
+        plan.append((lm_head, self._regions(wh)))
         return plan
 
     def _launch_step(self, stream):

@@ -57,12 +57,15 @@ def main():
             e.token.fill_(101)
         ps[0][0](stream)
         pt[0][0](stream)
-        cur = 1
+        cur = cur_s = 1
         for i in range(min(4, cfg.num_hidden_layers)):
-            for f, _ in ps[1 + 5 * i:6 + 5 * i]:
+            # with slices (single GPU) or p2p (tensor parallel), layer i's
+            # output is written by the next launch (layer i + 1's in_proj or
+            # the LM head)
+            end_s = 1 + 5 * (i + 1) + (1 if single.slices else 0)
+            for f, _ in ps[cur_s:end_s]:
                 f(stream)
-            # with p2p, layer i's output is written by the next launch (layer
-            # i + 1's in_proj or the LM head)
+            cur_s = end_s
             end = 1 + nl * (i + 1) + (1 if collective == "p2p" else 0)
             for f, _ in pt[cur:end]:
                 f(stream)
