@@ -178,3 +178,33 @@ def test_slices_count_out_of_range_is_reported():
         assert torch.equal(h2, res)  # one zero slice, or none
         outs.append(silu)
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+
+
+def test_slices_layer_boundaries():
+    """With slices, layer i's residual stream is written by the launch after
+    the layer (layer i + 1's in_proj): stepping the plan that one launch
+    further gives the bits of the residual-add plan after each layer (the
+    cursor tests/tp_worker.py uses for its layer-by-layer check)."""
+    from qwen35_b200.config import qwen35_tiny
+    from qwen35_b200.engine import Qwen35DecodeEngine
+    from qwen35_b200.weights import random_weights
+    cfg = qwen35_tiny()
+    w = random_weights(cfg, seed=8, device="cuda")
+    a = Qwen35DecodeEngine(cfg, w, max_seq=32, slices=False)
+    b = Qwen35DecodeEngine(cfg, w, max_seq=32, slices=True)
+    pa, pb = a._plan_step(), b._plan_step()
+    stream = torch.cuda.current_stream().cuda_stream
+    for e in (a, b):
+        e.token.fill_(42)
+    pa[0][0](stream)
+    pb[0][0](stream)
+    cur = 1
+    for i in range(cfg.num_hidden_layers):
+        for f, _ in pa[1 + 5 * i:6 + 5 * i]:
+            f(stream)
+        end = 1 + 5 * (i + 1) + 1
+        for f, _ in pb[cur:end]:
+            f(stream)
+        cur = end
+        torch.cuda.synchronize()
+        assert torch.equal(a.hidden, b.hidden), i
