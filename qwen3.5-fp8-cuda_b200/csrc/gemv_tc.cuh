@@ -171,7 +171,8 @@ __device__ __forceinline__ void tc_x_zero(int nxb, uint8_t* xbg) {
 
 // x -> B operand of K-blocks [kb0, kb0 + nxb) (warps 2..7, 192 threads;
 // named barrier 1).  Pass 1 reads x once (h = x + x2 for ADD_RMSNORM), sums
-// squares over the whole of K and stages the slice's blocks in shared
+// squares over the whole of K (only the slice's blocks are read when no
+// whole-vector norm follows) and stages the slice's blocks in shared
 // memory; pass 2 normalises, splits into E4M3 hi / lo and writes the
 // swizzled B operand.  CTA 0 also writes h2_out and, over every block, xn_out
 // (re-reading the blocks outside its slice).  XBLK: bytes per K-block of the
@@ -267,12 +268,16 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
       if (b >= kb0 && b < kb0 + nxb) reinterpret_cast<uint4*>(stg)[i - kb0 * 16] = v[j];
     }
   }
-  for (int base = t; !psum && base < nch; base += NT * MAXC) {
+  // Without a whole-vector norm (PRO_NONE, PRO_GATED_NORM) only the slice's
+  // own blocks are read.
+  const bool local = a.pro == PRO_NONE || a.pro == PRO_GATED_NORM;
+  const int c0 = local ? kb0 * 16 : 0, c1 = local ? (kb0 + nxb) * 16 : nch;
+  for (int base = c0 + t; !psum && base < c1; base += NT * MAXC) {
     uint4 v[MAXC], r[MAXC];
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
       const int i = base + j * NT;
-      if (i < nch) {
+      if (i < c1) {
         v[j] = __ldg(reinterpret_cast<const uint4*>(xin) + i);
         if (a.pro == PRO_ADD_RMSNORM) r[j] = __ldg(reinterpret_cast<const uint4*>(a.x2) + i);
         // gated norm: z of the slice's blocks in the same round trip as x
@@ -283,7 +288,7 @@ __device__ __forceinline__ void tc_x_prepare(const GemvArgs& a, int kb0, int nxb
 #pragma unroll
     for (int j = 0; j < MAXC; ++j) {
       const int i = base + j * NT;
-      if (i >= nch) continue;
+      if (i >= c1) continue;
       uint32_t* vw = reinterpret_cast<uint32_t*>(&v[j]);
       if (a.pro == PRO_ADD_RMSNORM) {
         const uint32_t* rw = reinterpret_cast<const uint32_t*>(&r[j]);
