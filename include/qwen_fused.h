@@ -159,7 +159,10 @@ int qwen_linear_resid(const void* x, const void* w, const void* s, int N, int K,
  * The next RMSNorm-prologue launch on this host thread, after
  * qwen_set_slices_input(slices, count, n, max_slices, res), builds its input
  * as bf16(res + bf16(sum of the slices in order)), writes it to the buffer
- * passed as its x (the residual stream) and normalises it. */
+ * passed as its x (the residual stream) and normalises it.  Tensor-core path
+ * only (128x128 block scales, K a multiple of 128, K >= 256, at least
+ * ceil(K / 4096) slices allowed): otherwise cudaErrorNotSupported, nothing
+ * launched. */
 int qwen_linear_slices(const void* x, const void* w, const void* s, int N, int K, int K_blk, float* slices,
                        int* count, int max_slices, cudaStream_t stream);
 int qwen_set_slices_input(const float* slices, const int* count, int n, int max_slices, const void* res);

@@ -236,3 +236,35 @@ def test_against_reference_kernel(lib, name, n, k):
     assert_close(yr.cpu(), o, what="reference kernel vs oracle")
     assert_close(y, o, what="ours vs oracle")
     assert float((bf16_ulp_diff(y, yr.cpu()) > 1).float().mean()) < 0.001
+
+
+@pytest.mark.parametrize("n,k", [(2560, 9216), (2560, 4096), (32, 2560), (1000, 2560)])
+def test_linear_slices(lib, n, k):
+    """qwen_linear_slices: the K-slice rows added in slice order are the GEMV
+    (oracle tolerance) and bit-equal to the last-CTA reduction of
+    qwen_linear_partial (both planners pick the same split at these shapes:
+    same cost model, the 16-slice cap does not bind).  Too small a slice cap
+    for K is refused before any launch."""
+    g = synth.gen(n + k)
+    x = synth.bf16_vector(k, g)
+    w, s32 = synth.fp8_weight(n, k, g)
+    s = s32.to(BF16)
+    kblk = ops.scale_mode(n, s)
+    xd, wd, sd = x.cuda(), w.cuda(), s.cuda()
+    buf = torch.full((16 * n,), float("nan"), device="cuda")
+    cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    yf = torch.empty(n, device="cuda")
+    assert lib.qwen_linear_slices(_p(xd), _p(wd), _p(sd), n, k, kblk, _p(buf), _p(cnt), 16, P(0)) == 0
+    assert lib.qwen_linear_partial(_p(xd), _p(wd), _p(sd), n, k, kblk, _p(yf), P(0)) == 0
+    torch.cuda.synchronize()
+    c = int(cnt.item())
+    assert 1 <= c <= 16
+    rows = buf[: c * n].view(c, n)
+    tot = torch.zeros(n, device="cuda")
+    for i in range(c):
+        tot += rows[i]
+    assert torch.equal(tot, yf)
+    assert_close(tot.cpu(), oracle_f32(x, w, s, kblk), what=f"slices {n}x{k}")
+    if k // 128 > 64:  # more than 32 K-blocks per slice needs 3+ slices
+        assert lib.qwen_linear_slices(_p(xd), _p(wd), _p(sd), n, k, kblk, _p(buf), _p(cnt), 2, P(0)) != 0
+        assert lib.qwen_last_error() != 0
