@@ -95,7 +95,10 @@ void layer_mid_attn(void* q_buf, void* k_buf, const void* v_buf, void* attn_out,
 
 /* Last error recorded by a call on this host thread, then cleared (0 = none). */
 int qwen_last_error(void);
-/* Read and clear the device error word set by a bounded wait that timed out. */
+/* Read and clear the device error word (first error wins): 1-4 a bounded wait
+ * on a copy or a stage timed out, 5 a device-side cache position outside
+ * [0, max_seq), 6 a tensor-parallel peer exchange timed out, 7 a K-slice
+ * count outside [1, max_slices]. */
 int qwen_get_device_error(unsigned int* out);
 /* Enable (default) or disable programmatic dependent launch in the engine entry points. */
 void qwen_set_pdl(int enable);
