@@ -481,11 +481,15 @@ def run_ours(args):
     if world == 1:
         # every config 0/1 decode GEMV shape alone (after the timed region)
         from qwen35_b200.profile_gemv import time_shapes
+        try:
+            rows = time_shapes(peak)
+        except Exception as exc:  # reported, never allowed to drop the line
+            rows = {"error": repr(exc)[:200]}
         line["gemv_shapes"] = {
             "unit": "us per launch; GB/s of algorithmic bytes; frac of the measured peak",
             "method": "CUDA graph of back-to-back launches over rotating weight copies; abi = "
                       "launch_gemv_v4_extern (no PDL), chained = qwen_linear_partial (PDL)",
-            "rows": time_shapes(peak)}
+            "rows": rows}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = run_cpu_baseline(cfg)
