@@ -892,31 +892,72 @@ static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[QWEN_ATTN_
 
 // Device address of g_attn_noalloc_scratch per device.  In host code the
 // array's name is only a host-side handle, so the address is looked up with
-// cudaGetSymbolAddress by the first call on each device (with that device
-// current) and cached here.
-static void* g_attn_noalloc_addr[64];
+// cudaGetSymbolAddress, with the device current, by the first call on each
+// device and cached together with the CUDA context it belongs to: a call under
+// another context (after cudaDeviceReset, or a new primary context) looks the
+// address up again instead of using a stale one.  The cache is guarded by a
+// mutex, so concurrent first calls from several host threads are safe.
+namespace {
+struct NoallocAddr {
+  void* ctx = nullptr;
+  void* addr = nullptr;
+};
+NoallocAddr g_attn_noalloc_addr[64];
+std::mutex g_attn_noalloc_mu;
+
+typedef int (*PFN_ctx_get_current)(void**);
+PFN_ctx_get_current ctx_get_current() {
+  static PFN_ctx_get_current fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_ctx_get_current>(f);
+  });
+  return fn;
+}
+
+// Address of the scratch array on the current device (looked up on first use
+// per device and context).
+cudaError_t attn_noalloc_base(unsigned char** base) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  PFN_ctx_get_current get = ctx_get_current();
+  if (!get) return cudaErrorInitializationError;
+  void* ctx = nullptr;  // null until the runtime has made a context current
+  if (get(&ctx) != 0) return cudaErrorInitializationError;
+  std::lock_guard<std::mutex> lock(g_attn_noalloc_mu);
+  NoallocAddr& slot = g_attn_noalloc_addr[dev];
+  if (!ctx || slot.ctx != ctx || !slot.addr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_attn_noalloc_scratch);  // initialises the context if needed
+    if (e != cudaSuccess) return e;
+    if (get(&ctx) != 0 || !ctx) return cudaErrorInitializationError;
+    slot.addr = addr;
+    slot.ctx = ctx;
+  }
+  *base = static_cast<unsigned char*>(slot.addr);
+  return cudaSuccess;
+}
+}  // namespace
 
 extern "C" int qwen_attn_decode_noalloc(const void* q_all, const void* k_new, const void* v_new,
                                         const float* q_norm, const float* k_norm, const float* cos,
                                         const float* sin, void* k_cache, void* v_cache, const int* pos, int max_seq,
                                         int n_heads, int n_kv_heads, int head_dim, int rotary_dim, float eps,
                                         int chunk, int nsplit, void* out, cudaStream_t stream) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  unsigned char* base = nullptr;
+  cudaError_t e = attn_noalloc_base(&base);
   if (e != cudaSuccess) return record(e);
-  if (dev < 0 || dev >= 64) return record(cudaErrorInvalidDevice);
-  if (!g_attn_noalloc_addr[dev]) {
-    void* addr = nullptr;
-    e = cudaGetSymbolAddress(&addr, g_attn_noalloc_scratch);
-    if (e != cudaSuccess) return record(e);
-    g_attn_noalloc_addr[dev] = addr;
-  }
   if (n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || nsplit < 1) return record(cudaErrorInvalidValue);
   const size_t part_bytes = (size_t)n_heads * (size_t)nsplit * (size_t)(head_dim + 2) * sizeof(float);
   const size_t count_off = (part_bytes + 255) / 256 * 256;
   const size_t need = count_off + (size_t)n_kv_heads * sizeof(unsigned);
   if (need > QWEN_ATTN_NOALLOC_SCRATCH_BYTES) return record(cudaErrorInvalidValue);
-  unsigned char* base = static_cast<unsigned char*>(g_attn_noalloc_addr[dev]);
   unsigned* counts = reinterpret_cast<unsigned*>(base + count_off);
   // The array keeps whatever the previous call left; the split counters must
   // start at zero, so clear them on the stream ahead of the kernel.

@@ -9,11 +9,13 @@ tolerance.  The full-size Qwen3.5-4B engine is checked for determinism
 (graph replay == eager) and finiteness.
 """
 
+import os
+
 import pytest
 import torch
 
 from oracle.model import OracleModel
-from parity import max_rel, rel_l2
+from parity import assert_close, max_rel, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -207,4 +209,9 @@ def test_slices_layer_boundaries():
             f(stream)
         cur = end
         torch.cuda.synchronize()
-        assert torch.equal(a.hidden, b.hidden), i
+        if "QWEN_TCW_MIN_MB" in os.environ:
+            # the forced N = 256 kernel may split the residual projections'
+            # K differently from the slices: same sums, another FP32 order
+            assert_close(b.hidden.cpu(), a.hidden.cpu().float(), what=f"layer {i}")
+        else:
+            assert torch.equal(a.hidden, b.hidden), i

@@ -193,7 +193,11 @@ def test_fp8_linear_dispatch():
     assert_close(y.cpu(), ref, what="gemm batch")
     y1 = qops.fp8_linear(x[:1].cuda(), w.cuda(), s.cuda())
     torch.cuda.synchronize()
-    assert torch.equal(y1.cpu()[0], y.cpu()[0])
+    if "QWEN_TCW_MIN_MB" in os.environ or "QWEN_GEMV_PATH" in os.environ:
+        # a forced GEMV kernel may split K differently from the GEMM
+        assert_close(y1.cpu()[0], ref[0], what="gemv row 0")
+    else:
+        assert torch.equal(y1.cpu()[0], y.cpu()[0])
 
 
 def test_invalid_arguments_launch_nothing(lib):
@@ -241,9 +245,12 @@ def test_against_reference_kernel(lib, name, n, k):
 @pytest.mark.parametrize("n,k", [(2560, 9216), (2560, 4096), (32, 2560), (1000, 2560)])
 def test_linear_slices(lib, n, k):
     """qwen_linear_slices: the K-slice rows added in slice order are the GEMV
-    (oracle tolerance) and bit-equal to the last-CTA reduction of
-    qwen_linear_partial (both planners pick the same split at these shapes:
-    same cost model, the 16-slice cap does not bind).  Too small a slice cap
+    (oracle tolerance).  On the default kernel choice they are also bit-equal
+    to the last-CTA reduction of qwen_linear_partial (both calls run the M = 128
+    kernel with the same split: same cost model, the 16-slice cap does not
+    bind).  With the kernel choice forced (QWEN_TCW_MIN_MB / QWEN_GEMV_PATH) the
+    partial may run on the N = 256 kernel with another split and summation
+    order, so only the oracle tolerance applies there.  Too small a slice cap
     for K is refused before any launch."""
     g = synth.gen(n + k)
     x = synth.bf16_vector(k, g)
@@ -263,7 +270,10 @@ def test_linear_slices(lib, n, k):
     tot = torch.zeros(n, device="cuda")
     for i in range(c):
         tot += rows[i]
-    assert torch.equal(tot, yf)
+    forced = "QWEN_TCW_MIN_MB" in os.environ or "QWEN_GEMV_PATH" in os.environ
+    if not forced:
+        assert torch.equal(tot, yf)
+    assert_close(yf.cpu(), oracle_f32(x, w, s, kblk), what=f"partial {n}x{k}")
     assert_close(tot.cpu(), oracle_f32(x, w, s, kblk), what=f"slices {n}x{k}")
     if k // 128 > 64:  # more than 32 K-blocks per slice needs 3+ slices
         assert lib.qwen_linear_slices(_p(xd), _p(wd), _p(sd), n, k, kblk, _p(buf), _p(cnt), 2, P(0)) != 0
