@@ -7,6 +7,10 @@
 //   out = softmax(q k^T / sqrt(D)) v in FP32, bf16(out * (1/sum));
 //   gated: out = bf16(out * bf16(sigmoid(gate))).
 //
+// Inputs produced earlier in the same step (q, gate, the new k / v, split
+// partials) are read at L2 (ld.global.cg), so the same code serves the
+// persistent step kernel, where an SM's L1 may hold an older layer's lines.
+//
 // Mapping: one CTA per (KV head, position split).  The CTA handles all G query
 // heads of its KV head, so each K/V row is read once for G heads.  The current
 // context (pos + 1 positions, known only on the device) is spread over the
@@ -56,7 +60,7 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
                                                int lane) {
   constexpr int EPL = D / 32;
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) v[e] = bf2f(src[lane * EPL + e]);
+  for (int e = 0; e < EPL; ++e) v[e] = bf2f(__ldcg(src + lane * EPL + e));
   if (norm_w) {
     float ss = 0.f;
 #pragma unroll
@@ -84,27 +88,28 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
   }
 }
 
-template <int D, int G>
-__global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+// One (KV head, split) unit of the attention step on ATTN_WARPS warps (threads
+// 0 .. ATTN_WARPS*32-1 of the caller, named barrier 1).  `asmem` holds
+// attn_smem_bytes<D, G>() bytes; `s_last` is one shared int.  Every exit is
+// uniform over the calling threads.  U: positions per warp in flight; QREG:
+// the scaled queries held in registers (else re-read from shared memory per
+// position, for callers with a tighter register budget).
+template <int D, int G, int U = 4, bool QREG = true>
+__device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, float* asmem, int* s_last_p) {
   constexpr int EPL = D / 32;
-  extern __shared__ __align__(16) float asmem[];
+  constexpr int NT = ATTN_WARPS * 32;
   float* qsm = asmem;                       // [G][D] scaled query
   float* wo = qsm + G * D;                  // [ATTN_WARPS][G][D]
   float* wm = wo + ATTN_WARPS * G * D;      // [ATTN_WARPS][G]
   float* wl = wm + ATTN_WARPS * G;          // [ATTN_WARPS][G]
   float* kv_sm = wl + ATTN_WARPS * G;       // [2][D] new k, v (fp32 of bf16 values)
   float* tmp = kv_sm + 2 * D;               // [ATTN_WARPS][D] rope scratch
-  __shared__ int s_last;
-
-  const int kh = blockIdx.x, split = blockIdx.y;
+  int& s_last = *s_last_p;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) pdl_trigger();
-  if (warp == 0) l2_prefetch_share(a.pf, lane);
-  pdl_wait();
 
-  const int pos = a.pos_ptr ? *a.pos_ptr : a.pos_const;
-  if (pos < 0 || pos >= a.max_seq) {  // uniform over the grid: every CTA leaves
-    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) qwen_err_set(ERR_POS_RANGE);
+  const int pos = a.pos_ptr ? __ldcg(a.pos_ptr) : a.pos_const;
+  if (pos < 0 || pos >= a.max_seq) {  // uniform over the grid: every unit leaves
+    if (threadIdx.x == 0 && kh == 0 && split == 0) qwen_err_set(ERR_POS_RANGE);
     return;
   }
   const int total = a.seq_len > 0 ? a.seq_len : pos + 1;
@@ -122,7 +127,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
         attn_prep_head<D>(src, a.q_norm, cs, sn, a.rot, a.eps, tmp + warp * D, v, lane);
       } else {
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) v[e] = bf2f(src[lane * EPL + e]);
+        for (int e = 0; e < EPL; ++e) v[e] = bf2f(__ldcg(src + lane * EPL + e));
       }
 #pragma unroll
       for (int e = 0; e < EPL; ++e) qsm[task * D + lane * EPL + e] = v[e] * qscale;
@@ -138,20 +143,22 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
     } else {
 #pragma unroll
       for (int e = 0; e < EPL; ++e) {
-        const bf16 x = a.v_new[(size_t)kh * D + lane * EPL + e];
+        const bf16 x = __ldcg(a.v_new + (size_t)kh * D + lane * EPL + e);
         kv_sm[D + lane * EPL + e] = bf2f(x);
         if (split == 0) a.v_cache[((size_t)kh * a.max_seq + pos) * D + lane * EPL + e] = x;
       }
     }
   }
-  __syncthreads();
+  named_bar(1, NT);
 
   // ---- Phase B: positions of this split ----
-  float qr[G][EPL];
+  float qr[QREG ? G : 1][EPL];
+  if constexpr (QREG) {
 #pragma unroll
-  for (int g = 0; g < G; ++g)
+    for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) qr[g][e] = qsm[g * D + lane * EPL + e];
+      for (int e = 0; e < EPL; ++e) qr[g][e] = qsm[g * D + lane * EPL + e];
+  }
   float m[G], l[G], o[G][EPL];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -167,7 +174,6 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
   const bf16* vbase = a.v_cache + (size_t)kh * a.max_seq * D;
   // Each warp takes U consecutive positions at a time and issues all their
   // K / V row loads (one vector load per lane and row) before using them.
-  constexpr int U = 4;
   auto load_row = [&](int p, uint32_t (&kr)[EPL / 2], uint32_t (&vr)[EPL / 2]) {
     const bf16* kp = kbase + (size_t)p * D + lane * EPL;
     const bf16* vp = vbase + (size_t)p * D + lane * EPL;
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
     for (int g = 0; g < G; ++g) {
       float dot = 0.f;
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) dot = fmaf(qr[g][e], kx[e], dot);
+      for (int e = 0; e < EPL; ++e) dot = fmaf(QREG ? qr[QREG ? g : 0][e] : qsm[g * D + lane * EPL + e], kx[e], dot);
       dot = warp_sum(dot);
       const float nm = fmaxf(m[g], dot);
       const float eo = expf(m[g] - nm);
@@ -235,11 +241,11 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
 #pragma unroll
     for (int e = 0; e < EPL; ++e) wo[(warp * G + g) * D + lane * EPL + e] = o[g][e];
   }
-  __syncthreads();
+  named_bar(1, NT);
 
   // Merge warps: thread handles (g, d) pairs.
   const int nsplit = a.nsplit;
-  for (int idx = threadIdx.x; idx < G * D; idx += ATTN_WARPS * 32) {
+  for (int idx = threadIdx.x; idx < G * D; idx += NT) {
     const int g = idx / D, d = idx % D;
     float M = -INFINITY;
     for (int w = 0; w < ATTN_WARPS; ++w) M = fmaxf(M, wm[w * G + g]);
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
       const float r = Os * (1.0f / Ls);
       bf16 ob = f2bf(r);
       if (a.gate) {
-        const float gv = bf2f(a.gate[(size_t)h * a.q_stride + d]);
+        const float gv = bf2f(__ldcg(a.gate + (size_t)h * a.q_stride + d));
         ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv))));
       }
       a.out[(size_t)h * D + d] = ob;
@@ -272,12 +278,12 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
   if (nsplit == 1) return;
 
   __threadfence();
-  __syncthreads();
+  named_bar(1, NT);
   if (threadIdx.x == 0) {
     const unsigned prev = atomicAdd(a.ws_count + kh, 1u);
     s_last = prev == (unsigned)(nsplit - 1);
   }
-  __syncthreads();
+  named_bar(1, NT);
   if (!s_last) return;
   __threadfence();
   const int n_active = (total + chunk - 1) / chunk;
@@ -304,8 +310,8 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
       if (lane == 0) wl[g] = L;
     }
   }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < G * D; idx += ATTN_WARPS * 32) {
+  named_bar(1, NT);
+  for (int idx = threadIdx.x; idx < G * D; idx += NT) {
     const int g = idx / D, d = idx % D;
     const int h = kh * G + g;
     const float* base = a.ws_part + (size_t)h * nsplit * (D + 2);
@@ -336,12 +342,22 @@ __global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __gr
     }
     bf16 ob = f2bf(Os * (1.0f / Ls));
     if (a.gate) {
-      const float gv = bf2f(a.gate[(size_t)h * a.q_stride + d]);
+      const float gv = bf2f(__ldcg(a.gate + (size_t)h * a.q_stride + d));
       ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv))));
     }
     a.out[(size_t)h * D + d] = ob;
   }
   if (threadIdx.x == 0) a.ws_count[kh] = 0u;
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(ATTN_WARPS * 32) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(16) float asmem[];
+  __shared__ int s_last;
+  if (threadIdx.x == 0) pdl_trigger();
+  if ((threadIdx.x >> 5) == 0) l2_prefetch_share(a.pf, threadIdx.x & 31);
+  pdl_wait();
+  attn_unit<D, G>(a, blockIdx.x, blockIdx.y, asmem, &s_last);
 }
 
 template <int D, int G>

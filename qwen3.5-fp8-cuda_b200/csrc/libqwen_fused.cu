@@ -967,3 +967,6 @@ extern "C" int qwen_attn_decode_noalloc(const void* q_all, const void* k_new, co
                           n_kv_heads, head_dim, rotary_dim, eps, chunk, nsplit, reinterpret_cast<float*>(base),
                           counts, out, stream);
 }
+
+// Persistent decode-step kernel (include/qwen_step.h).
+#include "step_host.cuh"

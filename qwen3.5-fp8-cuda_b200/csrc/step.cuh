@@ -1,0 +1,818 @@
+// Persistent decode-step kernel: one launch per token.
+//
+// The batch-1 decode step of the Qwen3.5 hybrid (main.py:1509-1604 with the
+// kernels of fused_kernels.cu) is a chain of ~160 dependent stages: grouped
+// GEMVs with fused prologues / epilogues, the GatedDeltaNet recurrent step,
+// decode attention and the LM head with greedy argmax.  Launched one kernel
+// per stage, every stage pays a kernel boundary and its weight stream stops
+// while the chain waits.  Here one cooperative grid (one CTA per SM) walks
+// the whole stage list:
+//
+//  * a producer warp per CTA streams the CTA's share of every stage's
+//    weights, in stage order, into a ring of shared-memory slots with 1-D bulk
+//    copies (cp.async.bulk, TMA engine, no multicast).  Weights are static, so
+//    the producer runs ahead across stage boundaries, limited only by the
+//    ring: while the chain waits for a stage's input, the HBM stream keeps
+//    filling the next stages' slots.  The GatedDeltaNet state of a head is
+//    streamed the same way by the CTA that owns the head;
+//  * eight consumer warps run the stages.  A stage starts once every CTA has
+//    finished the previous one (a per-stage arrival counter in global memory,
+//    release / acquire at GPU scope, every wait bounded by %globaltimer);
+//  * GEMV stages compute on the FP8 tensor cores (mma.sync m16n8k32 E4M3,
+//    FP32 accumulation): the weights are the A operand (16 rows x 32 K per
+//    MMA), x is the B operand with its E4M3 hi part in column 0 and lo part
+//    in column 1 (x * 2^e = hi + lo / 32 per 128-wide K block, exact for the
+//    BF16 values within 2^-14 of the block maximum), so one MMA gives both
+//    partial sums of 16 rows.  Scale x 2^-e is applied per 128-K block in
+//    FP32, as the reference's explicit dequantisation does (main.py:497-501).
+//
+// Weights are stored pre-packed for this kernel (qwen_step_pack): per 16-row
+// tile and 512-wide K chunk, 8 KB laid out so that one 16-byte shared load
+// per lane is exactly the lane's A fragments of two MMAs, followed by the
+// chunk's four FP32 block scales.  A chunk is one bulk copy.
+//
+// Summation order differs from the reference kernels (per-chunk tensor-core
+// sums, then chunk partials in order); products are exact and sums FP32, as
+// in the reference.  The result does not depend on timing: every sum is taken
+// in a fixed order.
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "gdn.cuh"
+#include "attn.cuh"
+
+namespace qwen {
+
+enum : int { ST_GEMV = 0, ST_GDN = 1, ST_ATTN = 2 };
+// x prologue of a GEMV stage
+enum : int {
+  STP_PLAIN = 0,        // x as given (BF16 vector)
+  STP_NORM = 1,         // x <- RMSNorm(1+w)(x)
+  STP_EMBED_NORM = 2,   // h <- table[*token] (CTA 0 stores h), x <- RMSNorm(1+w)(h)
+  STP_SLICES_NORM = 3,  // h <- bf16(res + bf16(sum of the slices, in order)) (CTA 0 stores h), x <- RMSNorm(1+w)(h)
+};
+enum : unsigned {
+  ERR_STEP_TIMEOUT = 8,  // a bounded wait of the step kernel gave up (the step was abandoned)
+  ERR_TOKEN_RANGE = 9,   // an embedding row index outside the table (row 0 used)
+};
+
+constexpr int ST_ROWS = 16;                    // weight rows per tile (the M of one MMA)
+constexpr int ST_KC = 512;                     // K per chunk
+constexpr int ST_WBYTES = ST_ROWS * ST_KC;     // 8192 weight bytes per chunk
+constexpr int ST_CHUNK = ST_WBYTES + 16;       // + four FP32 block scales
+constexpr int ST_SLOTS = 24;                   // ring slots of one chunk each
+constexpr int ST_CW = 8;                       // consumer warps
+constexpr int ST_NT = ST_CW * 32;
+constexpr int ST_THREADS = ST_NT + 32;         // + the producer warp
+constexpr int ST_MAXK = 9216;                  // longest GEMV input
+constexpr int ST_MAXB = (ST_MAXK / 128 + ST_CW - 1) / ST_CW;  // 128-blocks per warp in the prologue
+constexpr int ST_BATCH = 48;                   // chunk partials held before a reduction
+constexpr int ST_MAX_SEG = 4;
+constexpr int ST_ATTN_SLOTS = 6;               // contiguous scratch slots of an attention unit
+constexpr int ST_GDN_D = 128;                  // GatedDeltaNet head dim of the step kernel
+constexpr int ST_GDN_SLOTS = ST_GDN_D * ST_GDN_D * 4 / ST_WBYTES;  // 8: one head's FP32 state
+static_assert(ST_SLOTS % ST_ATTN_SLOTS == 0, "attention scratch groups must not wrap the ring");
+static_assert(ST_NT == ATTN_WARPS * 32, "attention units run on the consumer warps");
+
+// Shared memory plan (bytes from the dynamic shared memory base).
+struct StSmem {
+  static constexpr int ring = 0;
+  static constexpr int xh = ST_SLOTS * ST_CHUNK;
+  static constexpr int xl = xh + ST_MAXK;
+  static constexpr int xinv = xl + ST_MAXK;
+  static constexpr int part = xinv + ST_MAXK / 128 * 4;
+  static constexpr int red = part + ST_BATCH * ST_ROWS * 4;
+  static constexpr int misc = red + 64 * 4;
+  static constexpr int bars = misc + 32 * 8;
+  static constexpr int total = bars + 2 * ST_SLOTS * 8;
+};
+static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8 == 0, "alignment");
+static_assert(StSmem::total <= 227 * 1024, "shared memory");
+
+struct StStage {
+  int kind;
+  // GEMV
+  int K, C;            // input length; 512-wide chunks per tile row
+  int pro;
+  int nseg, pair, nslice, tiles, nunits, ipu;  // units = tiles x nslice; ipu = chunks (items) per unit
+  int x_rows;          // EMBED: rows of the table
+  const bf16* x;       // PLAIN / NORM input, EMBED table
+  const bf16* res;     // SLICES_NORM residual
+  const float* norm_w;
+  float eps;
+  bf16* h_out;         // EMBED / SLICES_NORM: the residual stream h (written by CTA 0)
+  const long long* token;
+  const float* sl_in;  // SLICES_NORM: [sl_in_count][sl_stride] FP32 partial rows
+  int sl_in_count, sl_stride;
+  float* sl_out;       // K-sliced output: [nslice][sl_rows]
+  int sl_rows;
+  unsigned long long* am_ws;        // ARGMAX: {key, count}, zero before the first step, left zeroed
+  unsigned long long* am_key_out;
+  long long* am_token_out;
+  int* pos_inc;
+  int seg_tile0[ST_MAX_SEG + 1];
+  GemvSeg seg[ST_MAX_SEG];          // w / w2: packed weights
+  // GatedDeltaNet: one unit per value head
+  GdnArgs gdn;
+  int gdn_heads;
+  // attention: one unit per (KV head, split)
+  AttnArgs attn;
+  int attn_dim, attn_g;
+};
+
+struct StProgram {
+  const StStage* stages;
+  int nstages;
+  unsigned* counters;    // [nstages + 1]: CTAs done with each stage, then with the step
+  unsigned* abort_flag;  // set by a timed-out wait; every wait then gives up at once
+  unsigned* timeline;    // optional [nstages][grid][ST_TL]: %globaltimer (low 32 bits, ns) per stage and CTA
+};
+
+// Timeline fields of one (stage, CTA): the consumers' wait for the previous
+// stage begins / ends, their work ends; the producer issues the stage's first
+// item / has issued its last one.
+enum : int { ST_TL_WAIT = 0, ST_TL_START = 1, ST_TL_END = 2, ST_TL_P0 = 3, ST_TL_P1 = 4, ST_TL = 5 };
+__device__ __forceinline__ void st_stamp(const StProgram& P, int s, int field) {
+  if (P.timeline) P.timeline[((size_t)s * gridDim.x + blockIdx.x) * ST_TL + field] = (unsigned)globaltimer_ns();
+}
+
+// ---------------------------------------------------------------------------
+// Waits and arrivals
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool st_aborted(const unsigned* abort_flag) {
+  return *reinterpret_cast<const volatile unsigned*>(abort_flag) != 0u;
+}
+__device__ __forceinline__ void st_abort(unsigned* abort_flag) {
+  qwen_err_set(ERR_STEP_TIMEOUT);
+  atomicExch(abort_flag, 1u);
+}
+
+// mbarrier phase wait, bounded by QWEN_WAIT_TIMEOUT_NS and by the abort flag.
+__device__ __forceinline__ bool st_mbar_wait(uint32_t bar, uint32_t parity, unsigned* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (st_aborted(abort_flag)) return false;
+    if (globaltimer_ns() - t0 > QWEN_WAIT_TIMEOUT_NS) {
+      st_abort(abort_flag);
+      return false;
+    }
+  }
+}
+
+// Wait until `count` CTAs have arrived at `counter` (acquire, GPU scope).
+__device__ __forceinline__ bool st_wait_count(const unsigned* counter, unsigned count, unsigned* abort_flag) {
+  if (ld_acquire_gpu_u32(counter) >= count) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i)
+      if (ld_acquire_gpu_u32(counter) >= count) return true;
+    if (st_aborted(abort_flag)) return false;
+    if (globaltimer_ns() - t0 > QWEN_WAIT_TIMEOUT_NS) {
+      st_abort(abort_flag);
+      return false;
+    }
+  }
+}
+
+// This CTA's contiguous share [u0, u1) of n units.
+__device__ __forceinline__ void st_range(int n, int& u0, int& u1) {
+  u0 = (int)(((long long)n * blockIdx.x) / gridDim.x);
+  u1 = (int)(((long long)n * (blockIdx.x + 1)) / gridDim.x);
+}
+__device__ __forceinline__ int st_attn_pad(uint32_t n) {
+  return (int)((ST_ATTN_SLOTS - n % ST_ATTN_SLOTS) % ST_ATTN_SLOTS);
+}
+__device__ __forceinline__ int st_find_seg(const StStage& S, int t) {
+  int sg = 0;
+#pragma unroll
+  for (int i = 1; i < ST_MAX_SEG; ++i)
+    if (i < S.nseg && t >= S.seg_tile0[i]) sg = i;
+  return sg;
+}
+
+// ---------------------------------------------------------------------------
+// Producer: one thread streams every item of this CTA, stage by stage.
+// Item m goes to slot m % ST_SLOTS; the slot's `full` barrier completes with
+// the copy, its `empty` barrier when the consumer has finished with it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, uint32_t full0, uint32_t empty0) {
+  const uint64_t pol = l2_policy_evict_first();
+  uint32_t n = 0;
+  bool ok = true;
+  auto acquire = [&](uint32_t& slot) -> bool {
+    slot = n % ST_SLOTS;
+    if (n >= (uint32_t)ST_SLOTS && !st_mbar_wait(empty0 + 8 * slot, ((n / ST_SLOTS) - 1) & 1u, P.abort_flag))
+      return false;
+    return true;
+  };
+  for (int s = 0; s < P.nstages && ok; ++s) {
+    const StStage& S = P.stages[s];
+    int u0, u1;
+    st_stamp(P, s, ST_TL_P0);
+    if (S.kind == ST_GEMV) {
+      // the stage's fields in registers: the copies below are asm with memory
+      // clobbers, after which the compiler would reload them from global memory
+      const int ns = S.nslice, ipu = S.ipu, pair = S.pair, nseg = S.nseg;
+      const size_t tile_bytes = (size_t)S.C * ST_CHUNK, slice_bytes = (size_t)(S.C / ns) * ST_CHUNK;
+      int t0[ST_MAX_SEG];
+      const uint8_t* wa[ST_MAX_SEG];
+      const uint8_t* wb[ST_MAX_SEG];
+#pragma unroll
+      for (int i = 0; i < ST_MAX_SEG; ++i) {
+        t0[i] = S.seg_tile0[i];
+        wa[i] = S.seg[i].w;
+        wb[i] = S.seg[i].w2;
+      }
+      st_range(S.nunits, u0, u1);
+      for (int u = u0; u < u1 && ok; ++u) {
+        const int t = u / ns, sl = u - t * ns;
+        const uint8_t* a = wa[0];
+        const uint8_t* b = wb[0];
+        int tb = t0[0];
+#pragma unroll
+        for (int i = 1; i < ST_MAX_SEG; ++i)
+          if (i < nseg && t >= t0[i]) {
+            a = wa[i];
+            b = wb[i];
+            tb = t0[i];
+          }
+        const size_t off = (size_t)(t - tb) * tile_bytes + (size_t)sl * slice_bytes;
+        a += off;
+        b = pair ? b + off : nullptr;
+        for (int i = 0; i < ipu; ++i) {
+          const uint8_t* src = pair ? ((i & 1) ? b : a) + (size_t)(i >> 1) * ST_CHUNK : a + (size_t)i * ST_CHUNK;
+          uint32_t slot;
+          if (!(ok = acquire(slot))) break;
+          mbar_arrive_expect_tx(full0 + 8 * slot, ST_CHUNK);
+          bulk_g2s(ring + slot * ST_CHUNK, src, ST_CHUNK, full0 + 8 * slot, pol);
+          ++n;
+        }
+      }
+    } else if (S.kind == ST_GDN) {
+      st_range(S.gdn_heads, u0, u1);
+      const uint8_t* state = reinterpret_cast<const uint8_t*>(S.gdn.state);
+      for (int h = u0; h < u1 && ok; ++h) {
+        const uint8_t* src = state + (size_t)h * ST_GDN_D * ST_GDN_D * 4;
+        for (int i = 0; i < ST_GDN_SLOTS; ++i) {
+          uint32_t slot;
+          if (!(ok = acquire(slot))) break;
+          mbar_arrive_expect_tx(full0 + 8 * slot, ST_WBYTES);
+          bulk_g2s(ring + slot * ST_CHUNK, src + (size_t)i * ST_WBYTES, ST_WBYTES, full0 + 8 * slot, pol);
+          ++n;
+        }
+      }
+    } else {  // ST_ATTN: scratch slots, no copy (a plain arrival completes the phase)
+      st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
+      for (int u = u0; u < u1 && ok; ++u) {
+        const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
+        for (int i = 0; i < cnt; ++i) {
+          uint32_t slot;
+          if (!(ok = acquire(slot))) break;
+          mbar_arrive(full0 + 8 * slot);
+          ++n;
+        }
+      }
+    }
+    st_stamp(P, s, ST_TL_P1);
+  }
+  // Drain: never leave the CTA with bulk copies in flight into its shared memory.
+  const uint32_t first = n > (uint32_t)ST_SLOTS ? n - ST_SLOTS : 0u;
+  for (uint32_t m = first; m < n; ++m) {
+    const uint32_t bar = full0 + 8 * (m % ST_SLOTS), par = (m / ST_SLOTS) & 1u;
+    if (mbar_try_wait(bar, par)) continue;
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, par)) {
+      if (globaltimer_ns() - t0 > QWEN_WAIT_TIMEOUT_NS) {
+        st_abort(P.abort_flag);
+        break;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// GEMV stage pieces
+// ---------------------------------------------------------------------------
+// x prologue (consumer threads, named barrier 1): the stage input in shared
+// memory as E4M3 hi (xh) and lo (xl) bytes per element and 2^-e per 128-K
+// block (xinv).  Warp w takes 128-blocks w, w + 8, ...; lane l elements
+// 4l .. 4l + 3 of each.  Inputs written earlier in the step are read at L2.
+__device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8_t* xl, float* xinv, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = S.K, nb = K >> 7, pro = S.pro, nsl = S.sl_in_count, sl_stride = S.sl_stride;
+  const float* sl_in = S.sl_in;
+  const bf16* xin = S.x;
+  if (pro == STP_EMBED_NORM) {
+    long long tok = __ldcg(S.token);
+    if (tok < 0 || tok >= S.x_rows) {
+      if (tid == 0 && blockIdx.x == 0) qwen_err_set(ERR_TOKEN_RANGE);
+      tok = 0;
+    }
+    xin += (size_t)tok * K;
+  }
+  const bf16* src = pro == STP_SLICES_NORM ? S.res : xin;
+  bf16* h_out = (blockIdx.x == 0 && (pro == STP_SLICES_NORM || pro == STP_EMBED_NORM)) ? S.h_out : nullptr;
+  float v[ST_MAXB][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < ST_MAXB; ++i) {
+    const int b = warp + i * ST_CW;
+    if (b >= nb) break;
+    const int k0 = b * 128 + lane * 4;
+    uint2 raw;
+    if (pro == STP_EMBED_NORM) {
+      raw = __ldg(reinterpret_cast<const uint2*>(src + k0));
+    } else {
+      raw = __ldcg(reinterpret_cast<const uint2*>(src + k0));
+    }
+    const float2 a01 = bf2x_to_f2(raw.x), a23 = bf2x_to_f2(raw.y);
+    v[i][0] = a01.x; v[i][1] = a01.y; v[i][2] = a23.x; v[i][3] = a23.y;
+    if (pro == STP_SLICES_NORM) {
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c = 0; c < nsl; ++c) {
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(sl_in + (size_t)c * sl_stride + k0));
+        sum[0] += p.x; sum[1] += p.y; sum[2] += p.z; sum[3] += p.w;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[i][q] = bfround(v[i][q] + bfround(sum[q]));
+    }
+    if (h_out) {
+      const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[i][0], v[i][1]);
+      const __nv_bfloat162 h23 = __floats2bfloat162_rn(v[i][2], v[i][3]);
+      uint2 hv;
+      hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+      hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+      *reinterpret_cast<uint2*>(h_out + k0) = hv;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ss = fmaf(v[i][q], v[i][q], ss);
+  }
+  const bool norm = pro != STP_PLAIN;
+  float rms = 1.f;
+  if (norm) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    named_bar(1, ST_NT);
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < ST_CW; ++i) tot += red[i];
+    rms = rsqrtf(tot / (float)K + S.eps);
+  }
+#pragma unroll
+  for (int i = 0; i < ST_MAXB; ++i) {
+    const int b = warp + i * ST_CW;
+    if (b >= nb) break;
+    const int k0 = b * 128 + lane * 4;
+    float x[4];
+    if (norm) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(S.norm_w + k0));
+      x[0] = bfround(v[i][0] * rms * (1.0f + w.x));
+      x[1] = bfround(v[i][1] * rms * (1.0f + w.y));
+      x[2] = bfround(v[i][2] * rms * (1.0f + w.z));
+      x[3] = bfround(v[i][3] * rms * (1.0f + w.w));
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) x[q] = v[i][q];
+    }
+    float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    m = warp_max(m);
+    // m = 1.f * 2^(ebits - 127): e = 134 - ebits puts m * 2^e in [2^7, 2^8)
+    const int ebits = (int)((__float_as_uint(m) >> 23) & 0xffu);
+    int e = m > 0.f ? (ebits == 0 ? 100 : 134 - ebits) : 0;
+    e = e < -100 ? -100 : (e > 100 ? 100 : e);
+    const float sc = exp2i(e);
+    float xs[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) xs[q] = x[q] * sc;
+    const uint32_t h01 = f32x2_to_e4m3x2(xs[0], xs[1]), h23 = f32x2_to_e4m3x2(xs[2], xs[3]);
+    const float2 g01 = h2u_to_f2(e4m3x2_to_f16x2(h01)), g23 = h2u_to_f2(e4m3x2_to_f16x2(h23));
+    // lo carries 32 * (x * 2^e - hi): |x * 2^e - hi| <= 8, so 32x stays below 448
+    const uint32_t l01 = f32x2_to_e4m3x2((xs[0] - g01.x) * 32.f, (xs[1] - g01.y) * 32.f);
+    const uint32_t l23 = f32x2_to_e4m3x2((xs[2] - g23.x) * 32.f, (xs[3] - g23.y) * 32.f);
+    *reinterpret_cast<uint32_t*>(xh + k0) = h01 | (h23 << 16);
+    *reinterpret_cast<uint32_t*>(xl + k0) = l01 | (l23 << 16);
+    if (lane == 0) xinv[b] = exp2i(-e);
+  }
+  named_bar(1, ST_NT);
+}
+
+// One chunk (16 rows x 512 K) on one warp: FP32 partial sums of rows g and
+// g + 8 (valid in lanes with lane % 4 == 0, g = lane / 4).
+__device__ __forceinline__ void st_chunk(const uint8_t* base, const uint8_t* xh, const uint8_t* xl, const float* xinv,
+                                         int c, int lane, float& acc0, float& acc1) {
+  const float4 sc = *reinterpret_cast<const float4*>(base + ST_WBYTES);
+  const float* xi = xinv + c * 4;
+  const float f[4] = {sc.x * xi[0], sc.y * xi[1], sc.z * xi[2], sc.w * xi[3]};
+  // B fragments: lanes 0-3 (column 0) the hi bytes, lanes 4-7 (column 1) the
+  // lo bytes of K [512c + 64j + 16(lane % 4), +16) for group j; other columns zero
+  uint4 xr[8];
+  if (lane < 8) {
+    const uint8_t* xs = (lane < 4 ? xh : xl) + c * ST_KC + (lane & 3) * 16;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr[j] = *reinterpret_cast<const uint4*>(xs + 64 * j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr[j] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  acc0 = 0.f;
+  acc1 = 0.f;
+  const uint8_t* wl = base + lane * 16;
+#pragma unroll
+  for (int kb = 0; kb < 4; ++kb) {
+    float d[4];
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int j = 2 * kb + jj;
+      const uint4 r0 = *reinterpret_cast<const uint4*>(wl + (2 * j) * 512);      // row g
+      const uint4 r1 = *reinterpret_cast<const uint4*>(wl + (2 * j + 1) * 512);  // row g + 8
+      if (jj == 0) {
+        mma_e4m3_zc(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
+      } else {
+        mma_e4m3(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
+      }
+      mma_e4m3(d, make_uint4(r0.z, r1.z, r0.w, r1.w), xr[j].z, xr[j].w);
+    }
+    acc0 = fmaf(f[kb], d[0] + d[1] * 0.03125f, acc0);
+    acc1 = fmaf(f[kb], d[2] + d[3] * 0.03125f, acc1);
+  }
+}
+
+// CTA-wide max of the running argmax keys, the cross-CTA maximum and its
+// finalisation by the last CTA (token, packed key, position increment).
+__device__ __forceinline__ void st_argmax_finish(const StStage& S, unsigned long long best,
+                                                 unsigned long long* misc) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = shfl_xor_u64(best, o);
+    best = other > best ? other : best;
+  }
+  if (lane == 0) misc[warp] = best;
+  named_bar(1, ST_NT);
+  if (tid == 0) {
+    best = 0;
+    for (int i = 0; i < ST_CW; ++i) best = misc[i] > best ? misc[i] : best;
+    unsigned long long* ws = S.am_ws;
+    if (best) atomicMax(ws, best);
+    __threadfence();
+    unsigned* cnt = reinterpret_cast<unsigned*>(ws + 1);
+    const unsigned prev = atomicAdd(cnt, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence();
+      const unsigned long long key = atomicAdd(ws, 0ull);
+      if (S.am_key_out) *S.am_key_out = key;
+      if (S.am_token_out) *S.am_token_out = (long long)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+      if (S.pos_inc) *S.pos_inc += 1;
+      *ws = 0ull;
+      *cnt = 0u;
+      __threadfence();
+    }
+  }
+}
+
+struct StCtx {
+  uint8_t* ring;
+  uint8_t* xh;
+  uint8_t* xl;
+  float* xinv;
+  float* part;
+  float* red;
+  unsigned long long* misc;
+  int* flag;
+  uint32_t full0, empty0;
+  unsigned* abort_flag;
+};
+
+__device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32_t& n) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int u0, u1;
+  st_range(S.nunits, u0, u1);
+  st_prologue(S, X.xh, X.xl, X.xinv, X.red);
+  const int ipu = S.ipu, nslice = S.nslice, pair = S.pair;
+  const int upb = ST_BATCH / ipu > 0 ? ST_BATCH / ipu : 1;
+  const int per = S.C / nslice;
+  unsigned long long am_best = 0;
+  bool good = true;
+  for (int ub = u0; ub < u1; ub += upb) {
+    const int ue = min(u1, ub + upb);
+    const int nit = (ue - ub) * ipu;
+    const uint32_t m0 = n + (uint32_t)(ub - u0) * ipu;
+    for (int q = warp; q < nit && good; q += ST_CW) {
+      const uint32_t m = m0 + q, slot = m % ST_SLOTS;
+      if (!st_mbar_wait(X.full0 + 8 * slot, (m / ST_SLOTS) & 1u, X.abort_flag)) {
+        good = false;
+        break;
+      }
+      const int u = ub + q / ipu, i = q % ipu;
+      const int t = u / nslice, sl = u - t * nslice;
+      const int c = sl * per + (pair ? (i >> 1) : i);
+      float a0, a1;
+      st_chunk(X.ring + slot * ST_CHUNK, X.xh, X.xl, X.xinv, c, lane, a0, a1);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(X.empty0 + 8 * slot);
+      if ((lane & 3) == 0) {
+        X.part[q * ST_ROWS + (lane >> 2)] = a0;
+        X.part[q * ST_ROWS + (lane >> 2) + 8] = a1;
+      }
+    }
+    named_bar(1, ST_NT);
+    for (int idx = tid; idx < (ue - ub) * ST_ROWS && good; idx += ST_NT) {
+      const int ul = idx / ST_ROWS, r = idx % ST_ROWS;
+      const int u = ub + ul;
+      const float* pp = X.part + ul * ipu * ST_ROWS + r;
+      float v = 0.f, v2 = 0.f;
+      if (pair) {
+        for (int i = 0; i < ipu; i += 2) {
+          v += pp[i * ST_ROWS];
+          v2 += pp[(i + 1) * ST_ROWS];
+        }
+      } else {
+        for (int i = 0; i < ipu; ++i) v += pp[i * ST_ROWS];
+      }
+      const int t = u / nslice, sl = u - t * nslice;
+      const int sg = st_find_seg(S, t);
+      const GemvSeg& G = S.seg[sg];
+      const int row = (t - S.seg_tile0[sg]) * ST_ROWS + r;
+      if (row >= G.n) continue;
+      if (S.sl_out) {
+        S.sl_out[(size_t)sl * S.sl_rows + row] = v;
+      } else {
+        am_best = gemv_epilogue(G, row, v, v2, am_best);
+      }
+    }
+    named_bar(1, ST_NT);
+  }
+  n += (uint32_t)(u1 - u0) * ipu;
+  if (S.am_ws) st_argmax_finish(S, am_best, X.misc);
+}
+
+// GatedDeltaNet step of one value head on the consumer warps: thread
+// (d = tid % 128, kg = tid / 128) keeps key rows [64 kg, 64 kg + 64) of value
+// column d in registers, read once from the ring (the state slots of the
+// head), and writes the updated column to global memory once.  Same
+// arithmetic as gdn_decode_kernel (the reference's delta_rule_decode_kernel,
+// fused_kernels.cu:623-684, plus the default path's gated RMSNorm,
+// main.py:1152-1159).
+__device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_t& n) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int D = ST_GDN_D;
+  const GdnArgs& a = S.gdn;
+  int u0, u1;
+  st_range(S.gdn_heads, u0, u1);
+  float* qs = X.part;
+  float* ks = X.part + D;
+  float* red2 = X.part + 2 * D;  // [2][D]
+  float* wsum = X.part + 4 * D;
+  for (int h = u0; h < u1; ++h) {
+    if (tid == 0) {
+      int ok = 1;
+      for (int i = 0; i < ST_GDN_SLOTS && ok; ++i) {
+        const uint32_t m = n + i;
+        if (!st_mbar_wait(X.full0 + 8 * (m % ST_SLOTS), (m / ST_SLOTS) & 1u, X.abort_flag)) ok = 0;
+      }
+      *X.flag = ok;
+    }
+    named_bar(1, ST_NT);
+    if (*X.flag) {
+      // every thread observes the completed phases itself (acquire of the
+      // bulk-copied state); they have completed, so each wait returns at once
+      for (int i = 0; i < ST_GDN_SLOTS; ++i) {
+        const uint32_t m = n + i;
+        for (int it = 0; it < (1 << 16) && !mbar_try_wait(X.full0 + 8 * (m % ST_SLOTS), (m / ST_SLOTS) & 1u); ++it) {
+        }
+      }
+      const int d = tid & (D - 1), kg = tid / D;
+      const int kh = h / a.rep;
+      float qv = 0.f, kv = 0.f;
+      if (tid < D) {
+        qv = bf2f(__ldcg(a.q + (size_t)kh * D + tid));
+        kv = bf2f(__ldcg(a.k + (size_t)kh * D + tid));
+      }
+      const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
+      if (lane == 0 && tid < D) {
+        X.red[warp] = sq;
+        X.red[4 + warp] = sk;
+      }
+      float s[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const int k = kg * 64 + i;
+        const uint32_t slot = (n + (k >> 4)) % ST_SLOTS;
+        s[i] = *reinterpret_cast<const float*>(X.ring + slot * ST_CHUNK + (k & 15) * (D * 4) + d * 4);
+      }
+      named_bar(1, ST_NT);
+      const float tq = X.red[0] + X.red[1] + X.red[2] + X.red[3];
+      const float tk = X.red[4] + X.red[5] + X.red[6] + X.red[7];
+      const float q_scale = rsqrtf(tq + 1e-6f) * rsqrtf((float)D);
+      const float k_scale = rsqrtf(tk + 1e-6f);
+      if (tid < D) {
+        qs[tid] = qv * q_scale;
+        ks[tid] = kv * k_scale;
+      }
+      named_bar(1, ST_NT);
+      const float decay = expf(__ldcg(a.g + h));
+      const float beta = bf2f(__ldcg(a.beta + h));
+      float pred = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) pred += s[i] * decay * ks[kg * 64 + i];
+      red2[kg * D + d] = pred;
+      named_bar(1, ST_NT);
+      const float ptot = red2[d] + red2[D + d];
+      const float delta = (bf2f(__ldcg(a.v + (size_t)h * D + d)) - ptot) * beta;
+      named_bar(1, ST_NT);  // red2 is read before it is reused
+      float o = 0.f;
+      float* Sg = a.state + (size_t)h * D * D;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const int k = kg * 64 + i;
+        const float u = s[i] * decay + ks[k] * delta;
+        Sg[(size_t)k * D + d] = u;
+        o += u * qs[k];
+      }
+      red2[kg * D + d] = o;
+      named_bar(1, ST_NT);
+      if (kg == 0) {
+        const bf16 core = f2bf(red2[d] + red2[D + d]);
+        bf16* out = a.out + (size_t)h * D + d;
+        if (!a.gated) {
+          *out = core;
+        } else {
+          const float c = bf2f(core);
+          const float cs = warp_sum(c * c);
+          if (lane == 0) wsum[warp] = cs;
+          named_bar(2, D);
+          const float var = (wsum[0] + wsum[1] + wsum[2] + wsum[3]) / (float)D;
+          const bf16 normed = f2bf(c * rsqrtf(var + a.eps));
+          const bf16 tv = f2bf(bf2f(normed) * bf2f(a.norm_w[d]));
+          const float zv = bf2f(__ldcg(a.z + (size_t)h * D + d));
+          const bf16 zs = f2bf(zv / (1.0f + expf(-zv)));
+          *out = f2bf(bf2f(tv) * bf2f(zs));
+        }
+      }
+    }
+    named_bar(1, ST_NT);
+    if (tid == 0)
+      for (int i = 0; i < ST_GDN_SLOTS; ++i) mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
+    n += ST_GDN_SLOTS;
+  }
+}
+
+// Attention units on the consumer warps, each over ST_ATTN_SLOTS contiguous
+// ring slots of scratch (aligned so they never wrap the ring).  Two positions
+// per warp in flight and the queries read from shared memory keep the unit
+// inside this kernel's register budget (9 warps: 168 registers a thread); each
+// head layout is a separate (not inlined) function with its own allocation.
+template <int D, int G>
+__device__ __noinline__ void st_attn_unit(const AttnArgs& a, int kh, int split, float* scratch, int* s_last) {
+  attn_unit<D, G, 2, false>(a, kh, split, scratch, s_last);
+}
+
+__device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32_t& n) {
+  const int tid = threadIdx.x;
+  int u0, u1;
+  st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
+  for (int u = u0; u < u1; ++u) {
+    const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
+    if (tid == 0) {
+      int ok = 1;
+      for (int i = 0; i < cnt && ok; ++i) {
+        const uint32_t m = n + i;
+        if (!st_mbar_wait(X.full0 + 8 * (m % ST_SLOTS), (m / ST_SLOTS) & 1u, X.abort_flag)) ok = 0;
+      }
+      *X.flag = ok;
+    }
+    named_bar(1, ST_NT);
+    if (*X.flag) {
+      float* scratch = reinterpret_cast<float*>(X.ring + ((n + cnt - ST_ATTN_SLOTS) % ST_SLOTS) * ST_CHUNK);
+      const int kh = u / S.attn.nsplit, split = u - kh * S.attn.nsplit;
+      int* s_last = X.flag + 1;
+#define QWEN_ST_ATTN(DD, GG) \
+  if (S.attn_dim == DD && S.attn_g == GG) st_attn_unit<DD, GG>(S.attn, kh, split, scratch, s_last);
+      QWEN_ST_ATTN(256, 1) else QWEN_ST_ATTN(256, 2) else QWEN_ST_ATTN(256, 4)
+      else QWEN_ST_ATTN(128, 1) else QWEN_ST_ATTN(128, 2) else QWEN_ST_ATTN(128, 4) else QWEN_ST_ATTN(128, 8)
+#undef QWEN_ST_ATTN
+    }
+    named_bar(1, ST_NT);
+    if (tid == 0)
+      for (int i = 0; i < cnt; ++i) mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
+    n += cnt;
+  }
+}
+
+__global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_constant__ StProgram P) {
+  extern __shared__ __align__(128) uint8_t st_smem[];
+  const uint32_t sbase = smem_u32(st_smem);
+  StCtx X;
+  X.ring = st_smem + StSmem::ring;
+  X.xh = st_smem + StSmem::xh;
+  X.xl = st_smem + StSmem::xl;
+  X.xinv = reinterpret_cast<float*>(st_smem + StSmem::xinv);
+  X.part = reinterpret_cast<float*>(st_smem + StSmem::part);
+  X.red = reinterpret_cast<float*>(st_smem + StSmem::red);
+  X.misc = reinterpret_cast<unsigned long long*>(st_smem + StSmem::misc);
+  X.flag = reinterpret_cast<int*>(X.misc + 16);
+  X.full0 = sbase + StSmem::bars;
+  X.empty0 = X.full0 + 8 * ST_SLOTS;
+  X.abort_flag = P.abort_flag;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST_SLOTS; ++i) {
+      mbar_init(X.full0 + 8 * i, 1);
+      mbar_init(X.empty0 + 8 * i, 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x >= ST_NT) {
+    if (threadIdx.x == ST_NT) st_producer(P, sbase + StSmem::ring, X.full0, X.empty0);
+    return;
+  }
+  const int tid = threadIdx.x;
+  uint32_t n = 0;
+  bool alive = true;
+  for (int s = 0; s < P.nstages; ++s) {
+    const StStage& S = P.stages[s];
+    if (tid == 0) st_stamp(P, s, ST_TL_WAIT);
+    if (s > 0) {
+      if (tid == 0) *X.flag = st_wait_count(P.counters + s - 1, gridDim.x, P.abort_flag) ? 1 : 0;
+      named_bar(1, ST_NT);
+      alive = *X.flag != 0;
+      named_bar(1, ST_NT);
+      if (!alive) break;
+    }
+    if (tid == 0) st_stamp(P, s, ST_TL_START);
+    const int kind = S.kind;
+    if (kind == ST_GEMV) {
+      st_gemv(S, X, n);
+    } else if (kind == ST_GDN) {
+      st_gdn(S, X, n);
+    } else {
+      st_attn(S, X, n);
+    }
+    named_bar(1, ST_NT);
+    if (tid == 0) {
+      st_stamp(P, s, ST_TL_END);
+      __threadfence();
+      atomicAdd(P.counters + s, 1u);
+    }
+  }
+  // End of the step: the last CTA clears the counters for the next launch
+  // (no CTA reads them again in this one).  After an abandoned step they stay
+  // as they are; the host clears them (qwen_step_reset).
+  if (tid == 0 && alive && !st_aborted(P.abort_flag)) {
+    __threadfence();
+    const unsigned prev = atomicAdd(P.counters + P.nstages, 1u);
+    if (prev == gridDim.x - 1) {
+      for (int i = 0; i <= P.nstages; ++i) P.counters[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Weight packing: [N, K] E4M3 row-major + block scales -> chunks of 16 rows x
+// 512 K.  Chunk (t, c) holds, for group j = 0..7 (64 K each) and half
+// h = 0, 1, the 512 bytes lane*16 + i = W[16t + 8h + lane/4][512c + 64j +
+// 16(lane%4) + i], then the FP32 scales of its four 128-K blocks (row block
+// 16t / 128).  Rows past N are zero.  One thread per 16 bytes.
+// ---------------------------------------------------------------------------
+template <typename ST>
+__global__ void step_pack_kernel(const uint8_t* __restrict__ w, const void* __restrict__ s, int N, int K, int kblk,
+                                 uint8_t* __restrict__ out) {
+  const int C = K / ST_KC;
+  const long long tiles = (N + ST_ROWS - 1) / ST_ROWS;
+  const long long total = tiles * C * (ST_WBYTES / 16 + 1);
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long chunk = idx / (ST_WBYTES / 16 + 1);
+    const int p = (int)(idx - chunk * (ST_WBYTES / 16 + 1));
+    const int t = (int)(chunk / C), c = (int)(chunk - (long long)t * C);
+    uint8_t* dst = out + chunk * ST_CHUNK;
+    if (p < ST_WBYTES / 16) {
+      const int j = p >> 6, h = (p >> 5) & 1, lane = p & 31;
+      const int row = t * ST_ROWS + 8 * h + (lane >> 2);
+      const int k = c * ST_KC + 64 * j + 16 * (lane & 3);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (row < N) v = *reinterpret_cast<const uint4*>(w + (size_t)row * K + k);
+      *reinterpret_cast<uint4*>(dst + p * 16) = v;
+    } else {
+      const int rb = (t * ST_ROWS) >> 7;
+      float f[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) f[i] = load_scale<ST>(s, rb * kblk + c * 4 + i);
+      *reinterpret_cast<float4*>(dst + ST_WBYTES) = make_float4(f[0], f[1], f[2], f[3]);
+    }
+  }
+}
+
+}  // namespace qwen

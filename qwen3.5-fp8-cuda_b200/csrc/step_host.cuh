@@ -1,0 +1,359 @@
+// Host side of the persistent decode-step kernel (include/qwen_step.h):
+// weight packing, program construction (unit partition of every stage,
+// K-slice choice, the stage array in device memory) and the cooperative
+// launch.  Included by libqwen_fused.cu after its status helpers.
+#pragma once
+
+#include "step.cuh"
+#include "../../include/qwen_step.h"
+
+#include <cmath>
+#include <cstdlib>
+#include <vector>
+
+namespace {
+
+struct StepProgramHost {
+  int dev = 0;
+  int grid = 0;
+  int nstages = 0;
+  qwen::StStage* d_stages = nullptr;
+  unsigned* d_counters = nullptr;  // nstages + 1 counters, then the abort flag
+  unsigned* timeline = nullptr;    // optional per-stage timestamps (qwen_step_set_timeline)
+};
+
+bool g_step_attr_done[64] = {};
+
+cudaError_t step_kernel_attr(int dev) {
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (g_step_attr_done[dev]) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(qwen::step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       qwen::StSmem::total);
+  if (e == cudaSuccess) g_step_attr_done[dev] = true;
+  return e;
+}
+
+// Weight of one extra K slice in the slice-count choice, in chunks (each
+// slice costs every CTA of the next stage one more FP32 row read at L2).
+double step_slice_cost() {
+  static double v = -1.0;
+  if (v < 0.0) {
+    const char* e = getenv("QWEN_STEP_SLICE_COST");
+    v = e ? atof(e) : 2.0;
+  }
+  return v;
+}
+
+// K slices of a single-segment EPI_SLICES stage: a divisor of C that
+// minimises the busiest CTA's chunks plus the slices' read cost.
+int step_choose_slices(int tiles, int C, int grid) {
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= C && s <= 16; ++s) {
+    if (C % s) continue;
+    const long long units = (long long)tiles * s;
+    const long long per_cta = (units + grid - 1) / grid;
+    const double cost = (double)(per_cta * (C / s)) + step_slice_cost() * s;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, const std::vector<qwen::StStage>& prev,
+                         const std::vector<qwen_step_stage>& prev_in) {
+  using namespace qwen;
+  o = StStage{};
+  o.kind = in.kind;
+  if (in.kind == QWEN_STEP_GEMV) {
+    if (in.K <= 0 || in.K % ST_KC || in.K > ST_MAXK || in.nseg < 1 || in.nseg > ST_MAX_SEG)
+      return cudaErrorInvalidValue;
+    if (in.pro < QWEN_STEP_PRO_PLAIN || in.pro > QWEN_STEP_PRO_SLICES_NORM) return cudaErrorInvalidValue;
+    if (in.pro != QWEN_STEP_PRO_SLICES_NORM && !in.x) return cudaErrorInvalidValue;
+    if (in.pro != QWEN_STEP_PRO_PLAIN && !in.norm_w) return cudaErrorInvalidValue;
+    if (in.pro == QWEN_STEP_PRO_EMBED_NORM && (!in.token || in.x_rows <= 0)) return cudaErrorInvalidValue;
+    if (in.pro == QWEN_STEP_PRO_SLICES_NORM && (!in.res || !in.sl_in || in.sl_stride < in.K))
+      return cudaErrorInvalidValue;
+    o.K = in.K;
+    o.C = in.K / ST_KC;
+    o.pro = in.pro;
+    o.nseg = in.nseg;
+    o.pair = in.pair ? 1 : 0;
+    o.x = static_cast<const bf16*>(in.x);
+    o.x_rows = in.x_rows;
+    o.res = static_cast<const bf16*>(in.res);
+    o.norm_w = in.norm_w;
+    o.eps = in.eps;
+    o.h_out = static_cast<bf16*>(in.h_out);
+    o.token = in.token;
+    o.sl_in = in.sl_in;
+    o.sl_stride = in.sl_stride;
+    o.sl_in_count = in.sl_in_count;
+    if (in.pro == QWEN_STEP_PRO_SLICES_NORM && o.sl_in_count <= 0) {
+      // the slice count of the latest earlier stage writing these rows
+      for (int i = (int)prev.size() - 1; i >= 0 && o.sl_in_count <= 0; --i)
+        if (prev_in[i].sl_out == in.sl_in) o.sl_in_count = prev[i].nslice;
+      if (o.sl_in_count <= 0) return cudaErrorInvalidValue;
+    }
+    if (o.sl_in_count > 16) return cudaErrorInvalidValue;
+    o.am_ws = in.am_ws;
+    o.am_key_out = in.am_key_out;
+    o.am_token_out = in.am_token_out;
+    o.pos_inc = in.pos_inc;
+    int tiles = 0;
+    bool slices = false, argmax = false;
+    for (int i = 0; i < in.nseg; ++i) {
+      const qwen_step_seg& s = in.seg[i];
+      if (!s.w || s.n <= 0 || (o.pair && !s.w2)) return cudaErrorInvalidValue;
+      switch (s.epi) {
+        case QWEN_STEP_EPI_STORE:
+        case QWEN_STEP_EPI_GATE_BETA:
+          if (!s.y) return cudaErrorInvalidValue;
+          break;
+        case QWEN_STEP_EPI_SILU_PAIR:
+          if (!s.y || !o.pair) return cudaErrorInvalidValue;
+          break;
+        case QWEN_STEP_EPI_ARGMAX:
+          argmax = true;
+          break;
+        case QWEN_STEP_EPI_CONV:
+          if (!s.y || !s.aux0 || !s.aux2 || s.cw < 1 || s.cw > 8) return cudaErrorInvalidValue;
+          break;
+        case QWEN_STEP_EPI_GATE_G:
+          if (!s.y || !s.aux0 || !s.aux1) return cudaErrorInvalidValue;
+          break;
+        case QWEN_STEP_EPI_SLICES:
+          slices = true;
+          break;
+        default:
+          return cudaErrorInvalidValue;
+      }
+      if (o.pair && s.epi != QWEN_STEP_EPI_SILU_PAIR) return cudaErrorInvalidValue;
+      GemvSeg& g = o.seg[i];
+      g = GemvSeg{};
+      g.w = static_cast<const uint8_t*>(s.w);
+      g.w2 = static_cast<const uint8_t*>(s.w2);
+      g.y = s.y;
+      g.y2 = s.y2;
+      g.aux0 = s.aux0;
+      g.aux1 = s.aux1;
+      g.aux2 = s.aux2;
+      g.n = s.n;
+      g.epi = s.epi == QWEN_STEP_EPI_SLICES ? EPI_SLICES : s.epi;
+      g.cw = s.cw;
+      g.row_offset = s.row_offset;
+      o.seg_tile0[i] = tiles;
+      tiles += (s.n + ST_ROWS - 1) / ST_ROWS;
+    }
+    for (int i = in.nseg; i <= ST_MAX_SEG; ++i) o.seg_tile0[i] = tiles;
+    if (slices && (in.nseg != 1 || !in.sl_out || in.sl_rows < in.seg[0].n)) return cudaErrorInvalidValue;
+    if (argmax && (!in.am_ws || in.nseg != 1)) return cudaErrorInvalidValue;
+    o.tiles = tiles;
+    int ns = 1;
+    if (slices) {
+      ns = in.nslice > 0 ? in.nslice : step_choose_slices(tiles, o.C, grid);
+      if (o.C % ns || ns > 16) return cudaErrorInvalidValue;
+      o.sl_out = in.sl_out;
+      o.sl_rows = in.sl_rows;
+    } else if (in.nslice > 1) {
+      return cudaErrorInvalidValue;
+    }
+    o.nslice = ns;
+    o.nunits = tiles * ns;
+    o.ipu = (o.C / ns) * (o.pair ? 2 : 1);
+    if (o.ipu > ST_BATCH) return cudaErrorInvalidValue;
+    return cudaSuccess;
+  }
+  if (in.kind == QWEN_STEP_GDN) {
+    if (in.g_dim != ST_GDN_D || in.g_heads <= 0 || in.g_rep <= 0 || !in.g_q || !in.g_k || !in.g_v || !in.g_g ||
+        !in.g_beta || !in.g_state || !in.g_out)
+      return cudaErrorInvalidValue;
+    if ((in.g_z == nullptr) != (in.g_norm_w == nullptr)) return cudaErrorInvalidValue;
+    GdnArgs& a = o.gdn;
+    a = GdnArgs{};
+    a.q = static_cast<const bf16*>(in.g_q);
+    a.k = static_cast<const bf16*>(in.g_k);
+    a.v = static_cast<const bf16*>(in.g_v);
+    a.g = in.g_g;
+    a.beta = static_cast<const bf16*>(in.g_beta);
+    a.state = in.g_state;
+    a.out = static_cast<bf16*>(in.g_out);
+    a.z = static_cast<const bf16*>(in.g_z);
+    a.norm_w = static_cast<const bf16*>(in.g_norm_w);
+    a.eps = in.g_eps;
+    a.rep = in.g_rep;
+    a.gated = in.g_z != nullptr;
+    o.gdn_heads = in.g_heads;
+    return cudaSuccess;
+  }
+  if (in.kind == QWEN_STEP_ATTN) {
+    if (in.a_kv <= 0 || in.a_heads <= 0 || in.a_heads % in.a_kv || in.a_nsplit < 1 || in.a_chunk < 1)
+      return cudaErrorInvalidValue;
+    if (!in.a_q || !in.a_k_new || !in.a_v_new || !in.a_k_cache || !in.a_v_cache || !in.a_pos || !in.a_out)
+      return cudaErrorInvalidValue;
+    if (in.a_nsplit > 1 && (!in.a_ws || !in.a_cnt)) return cudaErrorInvalidValue;
+    if (in.a_cos && (in.a_rot <= 0 || in.a_rot > in.a_dim || in.a_rot % 2)) return cudaErrorInvalidValue;
+    const int G = in.a_heads / in.a_kv;
+    const int smem = 4 * (G * in.a_dim + ATTN_WARPS * G * in.a_dim + 2 * ATTN_WARPS * G + 2 * in.a_dim +
+                          ATTN_WARPS * in.a_dim);
+    if (!((in.a_dim == 256 && (G == 1 || G == 2 || G == 4)) || (in.a_dim == 128 && (G == 1 || G == 2 || G == 4 || G == 8))) ||
+        smem > ST_ATTN_SLOTS * ST_CHUNK)
+      return cudaErrorInvalidValue;
+    AttnArgs& a = o.attn;
+    a = AttnArgs{};
+    a.q = static_cast<const bf16*>(in.a_q);
+    a.gate = a.q + in.a_dim;
+    a.k_new = static_cast<const bf16*>(in.a_k_new);
+    a.v_new = static_cast<const bf16*>(in.a_v_new);
+    a.q_norm = in.a_q_norm;
+    a.k_norm = in.a_k_norm;
+    a.cos = in.a_cos;
+    a.sin = in.a_sin;
+    a.k_cache = static_cast<bf16*>(in.a_k_cache);
+    a.v_cache = static_cast<bf16*>(in.a_v_cache);
+    a.pos_ptr = in.a_pos;
+    a.q_stride = 2 * in.a_dim;
+    a.max_seq = in.a_max_seq;
+    a.n_heads = in.a_heads;
+    a.n_kv = in.a_kv;
+    a.rot = in.a_rot;
+    a.eps = in.a_eps;
+    a.prep = 1;
+    a.chunk = in.a_chunk;
+    a.nsplit = in.a_nsplit;
+    a.ws_part = in.a_ws;
+    a.ws_count = in.a_cnt;
+    a.out = static_cast<bf16*>(in.a_out);
+    o.attn_dim = in.a_dim;
+    o.attn_g = G;
+    return cudaSuccess;
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t qwen_step_packed_bytes(int N, int K) {
+  if (N <= 0 || K <= 0 || K % qwen::ST_KC) return 0;
+  return (size_t)((N + qwen::ST_ROWS - 1) / qwen::ST_ROWS) * (size_t)(K / qwen::ST_KC) * qwen::ST_CHUNK;
+}
+
+int qwen_step_pack(const void* w, const void* s, int scale_f32, int N, int K, int K_blk, void* out,
+                   cudaStream_t stream) {
+  if (!w || !s || !out || N <= 0 || K <= 0 || K % qwen::ST_KC || K_blk != K / 128)
+    return record(cudaErrorInvalidValue);
+  const long long items = (long long)((N + 15) / 16) * (K / qwen::ST_KC) * (qwen::ST_WBYTES / 16 + 1);
+  const int block = 256;
+  const long long want = (items + block - 1) / block;
+  const int grid = (int)(want < 65535 ? want : 65535);
+  if (scale_f32)
+    qwen::step_pack_kernel<float><<<grid, block, 0, stream>>>(static_cast<const uint8_t*>(w), s, N, K, K_blk,
+                                                              static_cast<uint8_t*>(out));
+  else
+    qwen::step_pack_kernel<qwen::bf16><<<grid, block, 0, stream>>>(static_cast<const uint8_t*>(w), s, N, K, K_blk,
+                                                                   static_cast<uint8_t*>(out));
+  return record(cudaSuccess);
+}
+
+int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_out) {
+  if (!stages || nstages <= 0 || !program_out) return record(cudaErrorInvalidValue);
+  *program_out = nullptr;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record(e);
+  int sms = 0, coop = 0;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return record(e);
+  if ((e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev)) != cudaSuccess) return record(e);
+  if (!coop) return record(cudaErrorNotSupported);
+  if ((e = step_kernel_attr(dev)) != cudaSuccess) return record(e);
+  int per_sm = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qwen::step_kernel, qwen::ST_THREADS,
+                                                         qwen::StSmem::total)) != cudaSuccess)
+    return record(e);
+  if (per_sm < 1) return record(cudaErrorInvalidConfiguration);
+  const int grid = sms;  // one CTA per SM: the ring takes the SM's shared memory
+  std::vector<qwen::StStage> conv;
+  std::vector<qwen_step_stage> ins;
+  conv.reserve(nstages);
+  for (int i = 0; i < nstages; ++i) {
+    qwen::StStage o;
+    e = step_convert(stages[i], o, grid, conv, ins);
+    if (e != cudaSuccess) return record(e);
+    conv.push_back(o);
+    ins.push_back(stages[i]);
+  }
+  StepProgramHost* p = new StepProgramHost();
+  p->dev = dev;
+  p->grid = grid;
+  p->nstages = nstages;
+  e = cudaMalloc(&p->d_stages, sizeof(qwen::StStage) * nstages);
+  if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, sizeof(unsigned) * (nstages + 2));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(p->d_stages, conv.data(), sizeof(qwen::StStage) * nstages, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(p->d_counters, 0, sizeof(unsigned) * (nstages + 2));
+  if (e != cudaSuccess) {
+    cudaFree(p->d_stages);
+    cudaFree(p->d_counters);
+    delete p;
+    return record(e);
+  }
+  *program_out = p;
+  return 0;
+}
+
+int qwen_step_launch(void* program, cudaStream_t stream) {
+  StepProgramHost* p = static_cast<StepProgramHost*>(program);
+  if (!p) return record(cudaErrorInvalidValue);
+  qwen::StProgram P;
+  P.stages = p->d_stages;
+  P.nstages = p->nstages;
+  P.counters = p->d_counters;
+  P.abort_flag = p->d_counters + p->nstages + 1;
+  P.timeline = p->timeline;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p->grid);
+  cfg.blockDim = dim3(qwen::ST_THREADS);
+  cfg.dynamicSmemBytes = qwen::StSmem::total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return record(cudaLaunchKernelEx(&cfg, qwen::step_kernel, P));
+}
+
+int qwen_step_reset(void* program, cudaStream_t stream) {
+  StepProgramHost* p = static_cast<StepProgramHost*>(program);
+  if (!p) return record(cudaErrorInvalidValue);
+  return record(cudaMemsetAsync(p->d_counters, 0, sizeof(unsigned) * (p->nstages + 2), stream));
+}
+
+int qwen_step_destroy(void* program) {
+  StepProgramHost* p = static_cast<StepProgramHost*>(program);
+  if (!p) return 0;
+  cudaFree(p->d_stages);
+  cudaFree(p->d_counters);
+  delete p;
+  return 0;
+}
+
+int qwen_step_set_timeline(void* program, unsigned* timeline) {
+  StepProgramHost* p = static_cast<StepProgramHost*>(program);
+  if (!p) return record(cudaErrorInvalidValue);
+  p->timeline = timeline;
+  return 0;
+}
+
+int qwen_step_grid(void* program) {
+  StepProgramHost* p = static_cast<StepProgramHost*>(program);
+  return p ? p->grid : 0;
+}
+
+int qwen_step_smem_bytes(void) { return qwen::StSmem::total; }
+
+}  // extern "C"

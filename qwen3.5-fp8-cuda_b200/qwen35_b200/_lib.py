@@ -83,6 +83,16 @@ NEW_FUSED = {
     "qwen_set_p2p_input": (I, [P, P, I]),
     "qwen_gdn_decode_core": (I, [P, P, P, P, P, I, I, I, P]),
     "qwen_set_gated_input": (I, [P, P, F]),
+    # persistent decode step (include/qwen_step.h)
+    "qwen_step_packed_bytes": (ctypes.c_size_t, [I, I]),
+    "qwen_step_pack": (I, [P, P, I, I, I, I, P, P]),
+    "qwen_step_create": (I, [P, I, P]),
+    "qwen_step_launch": (I, [P, P]),
+    "qwen_step_reset": (I, [P, P]),
+    "qwen_step_destroy": (I, [P]),
+    "qwen_step_set_timeline": (I, [P, P]),
+    "qwen_step_grid": (I, [P]),
+    "qwen_step_smem_bytes": (I, []),
 }
 NEW_FP8 = {
     "qwen_fp8_last_error": (I, []),

@@ -1,0 +1,124 @@
+"""Stage timeline of the persistent decode-step kernel.
+
+    python -m qwen35_b200.profile_step [--layers N] [--context N] [--steps N] [--per-stage]
+
+Builds the random-init Qwen3.5-4B step engine (optionally with fewer layers),
+runs warm-up steps, then one step with the kernel's timeline on
+(``qwen_step_set_timeline``): per stage and CTA the consumers' wait for the
+previous stage begins / ends, their work ends, and the producer's first / last
+issue of the stage's items, all from ``%globaltimer``.  Prints, per stage
+name, where the step's time goes:
+
+* ``span``: from the previous stage's last CTA finishing to this stage's last
+  CTA finishing (the stage's share of the step's critical path);
+* ``sync``: from the previous stage's last CTA finishing to the median CTA
+  starting this stage (the cost of the grid-wide dependency);
+* ``work``: median and max over CTAs of the stage's own work;
+* ``lead``: how far ahead of the stage's start the median producer had
+  issued the stage's last item (negative: the stream was behind).
+
+Also prints the step time measured with CUDA events over ``--steps`` steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import statistics
+
+import torch
+
+KINDS = {0: "gemv", 1: "gdn", 2: "attn"}
+
+
+def stage_names(cfg):
+    """Short names of the engine's stages, in program order."""
+    names = []
+    for lt in cfg.layer_types:
+        names += ["qkv", "attn", "o_proj"] if lt == "full_attention" else ["in_proj", "gdn", "out_proj"]
+        names += ["gate_up", "down"]
+    names.append("lm_head")
+    return names
+
+
+def timeline(eng):
+    """One step with the timeline on: [stages, grid, 5] int64 ns from the earliest stamp."""
+    ns, grid = len(eng.stages), eng.grid
+    buf = torch.zeros(ns * grid * 5, dtype=torch.int32, device=eng.device)
+    eng.lib.qwen_step_set_timeline(eng.prog, ctypes.c_void_p(buf.data_ptr()))
+    eng.step()
+    torch.cuda.synchronize(eng.device)
+    eng.lib.qwen_step_set_timeline(eng.prog, ctypes.c_void_p(0))
+    t = (buf.cpu().to(torch.int64) & 0xFFFFFFFF).view(ns, grid, 5)
+    base = int(t[0, :, 0].min())
+    return (t - base) % (1 << 32)
+
+
+def summarize(cfg, t):
+    names = stage_names(cfg)
+    rows = []
+    prev_end = int(t[0, :, 0].min())
+    for s in range(t.shape[0]):
+        start, end, p1 = t[s, :, 1], t[s, :, 2], t[s, :, 4]
+        last_end = int(end.max())
+        work = (end - start).tolist()
+        rows.append(dict(stage=s, name=names[s] if s < len(names) else str(s), span=last_end - prev_end,
+                         sync=int(start.median()) - prev_end, work_med=statistics.median(work), work_max=max(work),
+                         lead=int(start.median()) - int(p1.median())))
+        prev_end = last_end
+    return rows
+
+
+def report(cfg, t, per_stage=False, out=print):
+    rows = summarize(cfg, t)
+    total = int(t[:, :, 2].max()) - int(t[0, :, 0].min())
+    out(f"timeline step: {total / 1000:.1f} us")
+    agg = {}
+    for r in rows:
+        a = agg.setdefault(r["name"], dict(n=0, span=0, sync=0, work_med=0, work_max=0, lead=0))
+        a["n"] += 1
+        for k in ("span", "sync", "work_med", "work_max", "lead"):
+            a[k] += r[k]
+    out(f"{'stage':10s} {'n':>4s} {'span us':>9s} {'share':>6s} {'sync us':>8s} {'work med':>9s} {'work max':>9s} "
+        f"{'lead us':>8s}  (per-stage means)")
+    for name, a in agg.items():
+        n = a["n"]
+        out(f"{name:10s} {n:4d} {a['span'] / n / 1000:9.2f} {a['span'] / total:6.1%} {a['sync'] / n / 1000:8.2f} "
+            f"{a['work_med'] / n / 1000:9.2f} {a['work_max'] / n / 1000:9.2f} {a['lead'] / n / 1000:8.2f}")
+    if per_stage:
+        for r in rows:
+            out(str(r))
+    return rows
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--context", type=int, default=128)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--per-stage", action="store_true")
+    args = ap.parse_args()
+    from .config import qwen35_4b
+    from .step import Qwen35StepEngine
+    from .weights import random_weights
+    cfg = qwen35_4b(num_hidden_layers=args.layers)
+    w = random_weights(cfg, seed=0, device="cuda")
+    eng = Qwen35StepEngine(cfg, w, max_seq=max(512, args.context + args.steps + 16))
+    eng.pos.fill_(args.context)
+    eng.token.fill_(7)
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        eng.step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    print(f"step: {ms * 1000:.1f} us ({1000 / ms:.1f} tok/s), {len(eng.stages)} stages, grid {eng.grid}")
+    report(cfg, timeline(eng), args.per_stage)
+
+
+if __name__ == "__main__":
+    main()

@@ -14,20 +14,32 @@ from conftest import REPO
 INCLUDE = os.path.join(REPO, "include")
 
 
+def _ctype_of(param: str):
+    """ctypes type of one C parameter declaration (pointers and streams are
+    c_void_p at this ABI)."""
+    p = param.strip()
+    if "*" in p or p.startswith("cudaStream_t"):
+        return ctypes.c_void_p
+    base = p.rsplit(None, 1)[0] if len(p.split()) > 1 else p
+    base = base.replace("const ", "").strip()
+    return {"int": ctypes.c_int, "float": ctypes.c_float, "unsigned long long": ctypes.c_ulonglong,
+            "unsigned int": ctypes.c_uint, "size_t": ctypes.c_size_t}[base]
+
+
 def header_functions(path):
-    """{name: n_params} for every function prototype in a header."""
+    """{name: [ctypes type per parameter]} for every function prototype in a header."""
     src = open(path).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     funcs = {}
-    for m in re.finditer(r"^\s*(?:void|int)\s+(\w+)\s*\(([^;{]*?)\)\s*;", src, flags=re.M | re.S):
+    for m in re.finditer(r"^\s*(?:void|int|size_t)\s+(\w+)\s*\(([^;{]*?)\)\s*;", src, flags=re.M | re.S):
         name, params = m.group(1), m.group(2).strip()
-        n = 0 if params in ("", "void") else params.count(",") + 1
-        funcs[name] = n
+        funcs[name] = [] if params in ("", "void") else [_ctype_of(x) for x in params.split(",")]
     return funcs
 
 
 HEADERS = {
     "qwen_fused.h": "libqwen_fused.so",
+    "qwen_step.h": "libqwen_fused.so",
     "qwen_fp8.h": "libqwen_fp8.so",
 }
 
@@ -43,15 +55,18 @@ def test_library_exports_every_declared_symbol(header):
 
 
 def test_ctypes_bindings_match_headers():
+    """Every binding's argtypes equal the header's parameter types one by one
+    (pointer and stream parameters as c_void_p)."""
     from qwen35_b200 import _lib
     fused = header_functions(os.path.join(INCLUDE, "qwen_fused.h"))
+    fused.update(header_functions(os.path.join(INCLUDE, "qwen_step.h")))
     fp8 = header_functions(os.path.join(INCLUDE, "qwen_fp8.h"))
     for name, argtypes in _lib.REFERENCE_FUSED_ARGTYPES.items():
-        assert fused[name] == len(argtypes), name
+        assert fused[name] == list(argtypes), name
     for name, (_, argtypes) in _lib.NEW_FUSED.items():
-        assert fused[name] == len(argtypes), name
+        assert fused[name] == list(argtypes), name
     for name, argtypes in _lib.REFERENCE_FP8_ARGTYPES.items():
-        assert fp8[name] == len(argtypes), name
+        assert fp8[name] == list(argtypes), name
     # every declared symbol is bound
     assert set(fused) == set(_lib.REFERENCE_FUSED_ARGTYPES) | set(_lib.NEW_FUSED)
     assert set(fp8) == set(_lib.REFERENCE_FP8_ARGTYPES) | set(_lib.NEW_FP8)
