@@ -70,7 +70,7 @@ typedef struct qwen_step_seg {
 typedef struct qwen_step_stage {
   int kind;              /* QWEN_STEP_GEMV / _GDN / _ATTN */
   /* GEMV */
-  int K;                 /* input length, a multiple of 512, at most 9216 */
+  int K;                 /* input length, a multiple of 512, at most 9216 (3072 unless PRO_PLAIN) */
   int pro;               /* QWEN_STEP_PRO_* */
   int nseg;              /* 1..4 segments over one shared input */
   int pair;              /* 1: every segment is a gate/up pair (SILU_PAIR) */
@@ -106,7 +106,8 @@ typedef struct qwen_step_stage {
   int g_heads;
   int g_dim;
   int g_rep;
-  /* attention (head dim 256 with 1, 2 or 4 query heads per KV head, or 128 with up to 8) */
+  /* attention (the Qwen3.5 layout: head dim 256, 4 query heads per KV head;
+     other layouts are refused with cudaErrorNotSupported) */
   const void* a_q;       /* BF16 [heads][2 * dim]: per head [q | gate] */
   const void* a_k_new;
   const void* a_v_new;
@@ -130,7 +131,7 @@ typedef struct qwen_step_stage {
   void* a_out;           /* BF16 [heads][dim] */
 } qwen_step_stage;
 
-/* Bytes of a packed [N, K] matrix: ceil(N/16) * (K/512) * 8208 (0 if K % 512). */
+/* Bytes of a packed [N, K] matrix: ceil(N/32) * (K/512) * 16400 (0 if K % 512). */
 size_t qwen_step_packed_bytes(int N, int K);
 
 /* Packs E4M3 weights w [N, K] with 128x128 block scales s ([ceil(N/128)][K/128],
@@ -151,10 +152,13 @@ int qwen_step_reset(void* program, cudaStream_t stream);
 
 int qwen_step_destroy(void* program);
 
-/* Profiling: launches record, per stage and CTA, five %globaltimer stamps
- * (low 32 bits, ns) into timeline [nstages][grid][5]: the consumers' wait for
- * the previous stage begins, ends, their work on the stage ends, the
- * producer issues the stage's first item, has issued its last.  Null stops it. */
+/* Profiling: launches record, per stage and CTA, eight words into timeline
+ * [nstages][grid][8]: five %globaltimer stamps (low 32 bits, ns) - the
+ * consumers' wait for the previous stage begins, ends, their work on the stage
+ * ends, the producer issues the stage's first item, has issued its last - then
+ * the producer's ns blocked on a full ring while issuing the stage, consumer
+ * warp 0's ns blocked on copies not yet landed, and the stamp at which a GEMV
+ * stage's x prologue was done.  Null stops it. */
 int qwen_step_set_timeline(void* program, unsigned* timeline);
 
 /* CTAs a launch uses (one per SM) and its dynamic shared memory in bytes. */

@@ -26,8 +26,8 @@
 //    partial sums of 16 rows.  Scale x 2^-e is applied per 128-K block in
 //    FP32, as the reference's explicit dequantisation does (main.py:497-501).
 //
-// Weights are stored pre-packed for this kernel (qwen_step_pack): per 16-row
-// tile and 512-wide K chunk, 8 KB laid out so that one 16-byte shared load
+// Weights are stored pre-packed for this kernel (qwen_step_pack): per 32-row
+// tile and 512-wide K chunk, 16 KB laid out so that one 16-byte shared load
 // per lane is exactly the lane's A fragments of two MMAs, followed by the
 // chunk's four FP32 block scales.  A chunk is one bulk copy.
 //
@@ -57,22 +57,32 @@ enum : unsigned {
   ERR_TOKEN_RANGE = 9,   // an embedding row index outside the table (row 0 used)
 };
 
-constexpr int ST_ROWS = 16;                    // weight rows per tile (the M of one MMA)
+constexpr int ST_ROWS = 32;                    // weight rows per tile (two MMA row groups of 16)
 constexpr int ST_KC = 512;                     // K per chunk
-constexpr int ST_WBYTES = ST_ROWS * ST_KC;     // 8192 weight bytes per chunk
+constexpr int ST_WBYTES = ST_ROWS * ST_KC;     // 16384 weight bytes per chunk
 constexpr int ST_CHUNK = ST_WBYTES + 16;       // + four FP32 block scales
-constexpr int ST_SLOTS = 24;                   // ring slots of one chunk each
+// Ring of chunk slots.  The bulk-copy engine's rate grows with the size of a
+// copy (measured on B200 through a 128-192 KB ring: 8 KB copies 5.2 TB/s,
+// 16 KB 6.4-6.8, 32 KB 6.9), hence 16 KB chunks.  The slot count is a
+// multiple of the consumer warps: items m and m + ST_SLOTS share a slot and
+// go to the same warp, so no thread ever waits on a phase beyond the next one
+// of a slot's barrier (a parity wait cannot tell those apart).
+constexpr int ST_SLOTS = 8;
 constexpr int ST_CW = 8;                       // consumer warps
 constexpr int ST_NT = ST_CW * 32;
 constexpr int ST_THREADS = ST_NT + 32;         // + the producer warp
 constexpr int ST_MAXK = 9216;                  // longest GEMV input
 constexpr int ST_MAXB = (ST_MAXK / 128 + ST_CW - 1) / ST_CW;  // 128-blocks per warp in the prologue
+constexpr int ST_NORM_MAXK = 3072;             // longest input of a normalising (or embedding) prologue
+constexpr int ST_NORM_MAXB = ST_NORM_MAXK / 128 / ST_CW;
 constexpr int ST_BATCH = 48;                   // chunk partials held before a reduction
 constexpr int ST_MAX_SEG = 4;
-constexpr int ST_ATTN_SLOTS = 6;               // contiguous scratch slots of an attention unit
+constexpr int ST_ATTN_SMEM = 48 * 1024;       // scratch of an attention unit
 constexpr int ST_GDN_D = 128;                  // GatedDeltaNet head dim of the step kernel
-constexpr int ST_GDN_SLOTS = ST_GDN_D * ST_GDN_D * 4 / ST_WBYTES;  // 8: one head's FP32 state
-static_assert(ST_SLOTS % ST_ATTN_SLOTS == 0, "attention scratch groups must not wrap the ring");
+constexpr int ST_GDN_SLOTS = ST_GDN_D * ST_GDN_D * 4 / ST_WBYTES;  // 4: one head's FP32 state
+constexpr int ST_GDN_KPS = ST_WBYTES / (ST_GDN_D * 4);            // 32 key rows of state per slot
+static_assert(ST_SLOTS % ST_CW == 0, "items m and m + ST_SLOTS must go to the same consumer warp");
+static_assert(ST_GDN_SLOTS <= ST_SLOTS, "a head's state must fit the ring");
 static_assert(ST_NT == ATTN_WARPS * 32, "attention units run on the consumer warps");
 
 // Shared memory plan (bytes from the dynamic shared memory base).
@@ -85,9 +95,11 @@ struct StSmem {
   static constexpr int red = part + ST_BATCH * ST_ROWS * 4;
   static constexpr int misc = red + 64 * 4;
   static constexpr int bars = misc + 32 * 8;
-  static constexpr int total = bars + 2 * ST_SLOTS * 8;
+  static constexpr int attn = (bars + 2 * ST_SLOTS * 8 + 127) / 128 * 128;
+  static constexpr int total = attn + ST_ATTN_SMEM;
 };
-static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8 == 0, "alignment");
+static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8 == 0 && StSmem::attn % 16 == 0,
+              "alignment");
 static_assert(StSmem::total <= 227 * 1024, "shared memory");
 
 struct StStage {
@@ -132,9 +144,18 @@ struct StProgram {
 // Timeline fields of one (stage, CTA): the consumers' wait for the previous
 // stage begins / ends, their work ends; the producer issues the stage's first
 // item / has issued its last one.
-enum : int { ST_TL_WAIT = 0, ST_TL_START = 1, ST_TL_END = 2, ST_TL_P0 = 3, ST_TL_P1 = 4, ST_TL = 5 };
+// Also, in ns: the producer's time blocked on a full ring while issuing the
+// stage, and consumer warp 0's time blocked on copies not yet landed.
+// Last, the stamp at which the stage's x prologue was done (GEMV stages).
+enum : int {
+  ST_TL_WAIT = 0, ST_TL_START = 1, ST_TL_END = 2, ST_TL_P0 = 3, ST_TL_P1 = 4, ST_TL_PBLOCK = 5, ST_TL_CBLOCK = 6,
+  ST_TL_PRO = 7, ST_TL = 8
+};
 __device__ __forceinline__ void st_stamp(const StProgram& P, int s, int field) {
   if (P.timeline) P.timeline[((size_t)s * gridDim.x + blockIdx.x) * ST_TL + field] = (unsigned)globaltimer_ns();
+}
+__device__ __forceinline__ void st_tl_put(unsigned* tl, int s, int field, unsigned v) {
+  if (tl) tl[((size_t)s * gridDim.x + blockIdx.x) * ST_TL + field] = v;
 }
 
 // ---------------------------------------------------------------------------
@@ -185,13 +206,19 @@ __device__ __forceinline__ bool st_wait_count(const unsigned* counter, unsigned 
   }
 }
 
+// Named barrier over `n` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n bar.red.and.pred po, %2, %3, pi;\n selp.u32 %0, 1, 0, po;\n}\n"
+      : "=r"(r) : "r"((uint32_t)v), "r"(id), "r"(n) : "memory");
+  return r != 0;
+}
+
 // This CTA's contiguous share [u0, u1) of n units.
 __device__ __forceinline__ void st_range(int n, int& u0, int& u1) {
   u0 = (int)(((long long)n * blockIdx.x) / gridDim.x);
   u1 = (int)(((long long)n * (blockIdx.x + 1)) / gridDim.x);
-}
-__device__ __forceinline__ int st_attn_pad(uint32_t n) {
-  return (int)((ST_ATTN_SLOTS - n % ST_ATTN_SLOTS) % ST_ATTN_SLOTS);
 }
 __device__ __forceinline__ int st_find_seg(const StStage& S, int t) {
   int sg = 0;
@@ -210,16 +237,22 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
   const uint64_t pol = l2_policy_evict_first();
   uint32_t n = 0;
   bool ok = true;
+  uint64_t blocked = 0;  // timeline only
   auto acquire = [&](uint32_t& slot) -> bool {
     slot = n % ST_SLOTS;
-    if (n >= (uint32_t)ST_SLOTS && !st_mbar_wait(empty0 + 8 * slot, ((n / ST_SLOTS) - 1) & 1u, P.abort_flag))
-      return false;
-    return true;
+    if (n < (uint32_t)ST_SLOTS) return true;
+    const uint32_t bar = empty0 + 8 * slot, par = ((n / ST_SLOTS) - 1) & 1u;
+    if (P.timeline ? mbar_test_wait(bar, par) : mbar_try_wait(bar, par)) return true;
+    const uint64_t t0 = P.timeline ? globaltimer_ns() : 0;
+    const bool r = st_mbar_wait(bar, par, P.abort_flag);
+    if (P.timeline) blocked += globaltimer_ns() - t0;
+    return r;
   };
   for (int s = 0; s < P.nstages && ok; ++s) {
     const StStage& S = P.stages[s];
     int u0, u1;
     st_stamp(P, s, ST_TL_P0);
+    blocked = 0;
     if (S.kind == ST_GEMV) {
       // the stage's fields in registers: the copies below are asm with memory
       // clobbers, after which the compiler would reload them from global memory
@@ -272,19 +305,9 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
           ++n;
         }
       }
-    } else {  // ST_ATTN: scratch slots, no copy (a plain arrival completes the phase)
-      st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
-      for (int u = u0; u < u1 && ok; ++u) {
-        const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
-        for (int i = 0; i < cnt; ++i) {
-          uint32_t slot;
-          if (!(ok = acquire(slot))) break;
-          mbar_arrive(full0 + 8 * slot);
-          ++n;
-        }
-      }
-    }
+    }  // ST_ATTN: no streamed items (the KV rows are read directly)
     st_stamp(P, s, ST_TL_P1);
+    st_tl_put(P.timeline, s, ST_TL_PBLOCK, (unsigned)blocked);
   }
   // Drain: never leave the CTA with bulk copies in flight into its shared memory.
   const uint32_t first = n > (uint32_t)ST_SLOTS ? n - ST_SLOTS : 0u;
@@ -308,10 +331,17 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
 // memory as E4M3 hi (xh) and lo (xl) bytes per element and 2^-e per 128-K
 // block (xinv).  Warp w takes 128-blocks w, w + 8, ...; lane l elements
 // 4l .. 4l + 3 of each.  Inputs written earlier in the step are read at L2.
+// Every load of a phase is issued before any is used: while the weight
+// stream saturates HBM an L2 round trip takes ~0.5 us, so dependent loads
+// would cost a round trip each.  MB: 128-blocks per warp this instantiation
+// holds (norm stages: K <= 3072).
+template <int MB>
 __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8_t* xl, float* xinv, float* red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = S.K, nb = K >> 7, pro = S.pro, nsl = S.sl_in_count, sl_stride = S.sl_stride;
   const float* sl_in = S.sl_in;
+  const float* norm_w = S.norm_w;
+  const bool norm = pro != STP_PLAIN;
   const bf16* xin = S.x;
   if (pro == STP_EMBED_NORM) {
     long long tok = __ldcg(S.token);
@@ -323,30 +353,63 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   }
   const bf16* src = pro == STP_SLICES_NORM ? S.res : xin;
   bf16* h_out = (blockIdx.x == 0 && (pro == STP_SLICES_NORM || pro == STP_EMBED_NORM)) ? S.h_out : nullptr;
-  float v[ST_MAXB][4];
-  float ss = 0.f;
+  // phase 1: input (or residual) and norm weights, all in flight
+  uint2 raw[MB];
+  float4 wv[MB];
 #pragma unroll
-  for (int i = 0; i < ST_MAXB; ++i) {
+  for (int i = 0; i < MB; ++i) {
     const int b = warp + i * ST_CW;
-    if (b >= nb) break;
     const int k0 = b * 128 + lane * 4;
-    uint2 raw;
-    if (pro == STP_EMBED_NORM) {
-      raw = __ldg(reinterpret_cast<const uint2*>(src + k0));
-    } else {
-      raw = __ldcg(reinterpret_cast<const uint2*>(src + k0));
+    if (b < nb) {
+      raw[i] = pro == STP_EMBED_NORM ? __ldg(reinterpret_cast<const uint2*>(src + k0))
+                                     : __ldcg(reinterpret_cast<const uint2*>(src + k0));
+      if (norm) wv[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k0));
     }
-    const float2 a01 = bf2x_to_f2(raw.x), a23 = bf2x_to_f2(raw.y);
+  }
+  float v[MB][4];
+#pragma unroll
+  for (int i = 0; i < MB; ++i) {
+    const float2 a01 = bf2x_to_f2(raw[i].x), a23 = bf2x_to_f2(raw[i].y);
     v[i][0] = a01.x; v[i][1] = a01.y; v[i][2] = a23.x; v[i][3] = a23.y;
-    if (pro == STP_SLICES_NORM) {
-      float sum[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int c = 0; c < nsl; ++c) {
-        const float4 p = __ldcg(reinterpret_cast<const float4*>(sl_in + (size_t)c * sl_stride + k0));
-        sum[0] += p.x; sum[1] += p.y; sum[2] += p.z; sum[3] += p.w;
+  }
+  // phase 2: the K-slice partial rows, two slices' loads in flight at a
+  // time, added in slice order
+  if (pro == STP_SLICES_NORM) {
+    float sum[MB][4];
+#pragma unroll
+    for (int i = 0; i < MB; ++i) sum[i][0] = sum[i][1] = sum[i][2] = sum[i][3] = 0.f;
+    for (int c = 0; c < nsl; c += 2) {
+      const bool two = c + 1 < nsl;
+      float4 p0[MB], p1[MB];
+#pragma unroll
+      for (int i = 0; i < MB; ++i) {
+        const int b = warp + i * ST_CW;
+        const float* pp = sl_in + (size_t)c * sl_stride + b * 128 + lane * 4;
+        if (b < nb) {
+          p0[i] = __ldcg(reinterpret_cast<const float4*>(pp));
+          if (two) p1[i] = __ldcg(reinterpret_cast<const float4*>(pp + sl_stride));
+        }
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) v[i][q] = bfround(v[i][q] + bfround(sum[q]));
+      for (int i = 0; i < MB; ++i) {
+        if (warp + i * ST_CW >= nb) continue;
+        sum[i][0] += p0[i].x; sum[i][1] += p0[i].y; sum[i][2] += p0[i].z; sum[i][3] += p0[i].w;
+        if (two) {
+          sum[i][0] += p1[i].x; sum[i][1] += p1[i].y; sum[i][2] += p1[i].z; sum[i][3] += p1[i].w;
+        }
+      }
     }
+#pragma unroll
+    for (int i = 0; i < MB; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[i][q] = bfround(v[i][q] + bfround(sum[i][q]));
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MB; ++i) {
+    const int b = warp + i * ST_CW;
+    if (b >= nb) continue;
+    const int k0 = b * 128 + lane * 4;
     if (h_out) {
       const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[i][0], v[i][1]);
       const __nv_bfloat162 h23 = __floats2bfloat162_rn(v[i][2], v[i][3]);
@@ -358,7 +421,6 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
 #pragma unroll
     for (int q = 0; q < 4; ++q) ss = fmaf(v[i][q], v[i][q], ss);
   }
-  const bool norm = pro != STP_PLAIN;
   float rms = 1.f;
   if (norm) {
     ss = warp_sum(ss);
@@ -370,13 +432,13 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
     rms = rsqrtf(tot / (float)K + S.eps);
   }
 #pragma unroll
-  for (int i = 0; i < ST_MAXB; ++i) {
+  for (int i = 0; i < MB; ++i) {
     const int b = warp + i * ST_CW;
-    if (b >= nb) break;
+    if (b >= nb) continue;  // warp-uniform
     const int k0 = b * 128 + lane * 4;
     float x[4];
     if (norm) {
-      const float4 w = __ldg(reinterpret_cast<const float4*>(S.norm_w + k0));
+      const float4 w = wv[i];
       x[0] = bfround(v[i][0] * rms * (1.0f + w.x));
       x[1] = bfround(v[i][1] * rms * (1.0f + w.y));
       x[2] = bfround(v[i][2] * rms * (1.0f + w.z));
@@ -407,10 +469,11 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   named_bar(1, ST_NT);
 }
 
-// One chunk (16 rows x 512 K) on one warp: FP32 partial sums of rows g and
-// g + 8 (valid in lanes with lane % 4 == 0, g = lane / 4).
+// One chunk (32 rows x 512 K) on one warp: FP32 partial sums of rows
+// 16 rg + g and 16 rg + g + 8 (rg = 0, 1) in acc[2 rg], acc[2 rg + 1], valid
+// in lanes with lane % 4 == 0 (g = lane / 4).
 __device__ __forceinline__ void st_chunk(const uint8_t* base, const uint8_t* xh, const uint8_t* xl, const float* xinv,
-                                         int c, int lane, float& acc0, float& acc1) {
+                                         int c, int lane, float (&acc)[4]) {
   const float4 sc = *reinterpret_cast<const float4*>(base + ST_WBYTES);
   const float* xi = xinv + c * 4;
   const float f[4] = {sc.x * xi[0], sc.y * xi[1], sc.z * xi[2], sc.w * xi[3]};
@@ -425,26 +488,35 @@ __device__ __forceinline__ void st_chunk(const uint8_t* base, const uint8_t* xh,
 #pragma unroll
     for (int j = 0; j < 8; ++j) xr[j] = make_uint4(0u, 0u, 0u, 0u);
   }
-  acc0 = 0.f;
-  acc1 = 0.f;
-  const uint8_t* wl = base + lane * 16;
+#pragma unroll 1
+  for (int rg = 0; rg < 2; ++rg) {  // one row group's loads live at a time (register budget)
+    const uint8_t* wl = base + rg * 8192 + lane * 16;
+    float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-  for (int kb = 0; kb < 4; ++kb) {
-    float d[4];
+    for (int kb = 0; kb < 4; ++kb) {
+      float d[4];
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int j = 2 * kb + jj;
-      const uint4 r0 = *reinterpret_cast<const uint4*>(wl + (2 * j) * 512);      // row g
-      const uint4 r1 = *reinterpret_cast<const uint4*>(wl + (2 * j + 1) * 512);  // row g + 8
-      if (jj == 0) {
-        mma_e4m3_zc(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
-      } else {
-        mma_e4m3(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * kb + jj;
+        const uint4 r0 = *reinterpret_cast<const uint4*>(wl + (2 * j) * 512);      // row g
+        const uint4 r1 = *reinterpret_cast<const uint4*>(wl + (2 * j + 1) * 512);  // row g + 8
+        if (jj == 0) {
+          mma_e4m3_zc(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
+        } else {
+          mma_e4m3(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
+        }
+        mma_e4m3(d, make_uint4(r0.z, r1.z, r0.w, r1.w), xr[j].z, xr[j].w);
       }
-      mma_e4m3(d, make_uint4(r0.z, r1.z, r0.w, r1.w), xr[j].z, xr[j].w);
+      a0 = fmaf(f[kb], d[0] + d[1] * 0.03125f, a0);
+      a1 = fmaf(f[kb], d[2] + d[3] * 0.03125f, a1);
     }
-    acc0 = fmaf(f[kb], d[0] + d[1] * 0.03125f, acc0);
-    acc1 = fmaf(f[kb], d[2] + d[3] * 0.03125f, acc1);
+    if (rg == 0) {
+      acc[0] = a0;
+      acc[1] = a1;
+    } else {
+      acc[2] = a0;
+      acc[3] = a1;
+    }
   }
 }
 
@@ -490,40 +562,56 @@ struct StCtx {
   float* red;
   unsigned long long* misc;
   int* flag;
+  float* attn;         // ST_ATTN_SMEM bytes of attention scratch
   uint32_t full0, empty0;
   unsigned* abort_flag;
+  unsigned* timeline;  // optional (see StProgram)
+  int stage;           // index of the stage being run (timeline)
 };
 
 __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32_t& n) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int u0, u1;
   st_range(S.nunits, u0, u1);
-  st_prologue(S, X.xh, X.xl, X.xinv, X.red);
+  if (S.pro == STP_PLAIN)
+    st_prologue<ST_MAXB>(S, X.xh, X.xl, X.xinv, X.red);
+  else
+    st_prologue<ST_NORM_MAXB>(S, X.xh, X.xl, X.xinv, X.red);
+  if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_PRO, (unsigned)globaltimer_ns());
   const int ipu = S.ipu, nslice = S.nslice, pair = S.pair;
   const int upb = ST_BATCH / ipu > 0 ? ST_BATCH / ipu : 1;
   const int per = S.C / nslice;
   unsigned long long am_best = 0;
   bool good = true;
+  uint64_t blocked = 0;  // timeline only: warp 0's wait for copies to land
   for (int ub = u0; ub < u1; ub += upb) {
     const int ue = min(u1, ub + upb);
     const int nit = (ue - ub) * ipu;
     const uint32_t m0 = n + (uint32_t)(ub - u0) * ipu;
     for (int q = warp; q < nit && good; q += ST_CW) {
       const uint32_t m = m0 + q, slot = m % ST_SLOTS;
-      if (!st_mbar_wait(X.full0 + 8 * slot, (m / ST_SLOTS) & 1u, X.abort_flag)) {
-        good = false;
-        break;
+      if (!(X.timeline ? mbar_test_wait(X.full0 + 8 * slot, (m / ST_SLOTS) & 1u)
+                       : mbar_try_wait(X.full0 + 8 * slot, (m / ST_SLOTS) & 1u))) {
+        const uint64_t t0 = X.timeline ? globaltimer_ns() : 0;
+        if (!st_mbar_wait(X.full0 + 8 * slot, (m / ST_SLOTS) & 1u, X.abort_flag)) {
+          good = false;
+          break;
+        }
+        if (X.timeline) blocked += globaltimer_ns() - t0;
       }
       const int u = ub + q / ipu, i = q % ipu;
       const int t = u / nslice, sl = u - t * nslice;
       const int c = sl * per + (pair ? (i >> 1) : i);
-      float a0, a1;
-      st_chunk(X.ring + slot * ST_CHUNK, X.xh, X.xl, X.xinv, c, lane, a0, a1);
+      float acc[4];
+      st_chunk(X.ring + slot * ST_CHUNK, X.xh, X.xl, X.xinv, c, lane, acc);
       __syncwarp();
       if (lane == 0) mbar_arrive(X.empty0 + 8 * slot);
       if ((lane & 3) == 0) {
-        X.part[q * ST_ROWS + (lane >> 2)] = a0;
-        X.part[q * ST_ROWS + (lane >> 2) + 8] = a1;
+        float* pq = X.part + q * ST_ROWS + (lane >> 2);
+        pq[0] = acc[0];
+        pq[8] = acc[1];
+        pq[16] = acc[2];
+        pq[24] = acc[3];
       }
     }
     named_bar(1, ST_NT);
@@ -554,6 +642,7 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
     named_bar(1, ST_NT);
   }
   n += (uint32_t)(u1 - u0) * ipu;
+  if (tid == 0) st_tl_put(X.timeline, X.stage, ST_TL_CBLOCK, (unsigned)blocked);
   if (S.am_ws) st_argmax_finish(S, am_best, X.misc);
 }
 
@@ -594,11 +683,19 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
       }
       const int d = tid & (D - 1), kg = tid / D;
       const int kh = h / a.rep;
-      float qv = 0.f, kv = 0.f;
+      // every global load of the head at once (one L2 round trip)
+      float qv = 0.f, kv = 0.f, zv = 0.f, nwv = 0.f;
       if (tid < D) {
         qv = bf2f(__ldcg(a.q + (size_t)kh * D + tid));
         kv = bf2f(__ldcg(a.k + (size_t)kh * D + tid));
+        if (a.gated) {
+          zv = bf2f(__ldcg(a.z + (size_t)h * D + d));
+          nwv = bf2f(a.norm_w[d]);
+        }
       }
+      const float gval = __ldcg(a.g + h);
+      const float bval = bf2f(__ldcg(a.beta + h));
+      const float vval = bf2f(__ldcg(a.v + (size_t)h * D + d));
       const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
       if (lane == 0 && tid < D) {
         X.red[warp] = sq;
@@ -608,8 +705,8 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const int k = kg * 64 + i;
-        const uint32_t slot = (n + (k >> 4)) % ST_SLOTS;
-        s[i] = *reinterpret_cast<const float*>(X.ring + slot * ST_CHUNK + (k & 15) * (D * 4) + d * 4);
+        const uint32_t slot = (n + k / ST_GDN_KPS) % ST_SLOTS;
+        s[i] = *reinterpret_cast<const float*>(X.ring + slot * ST_CHUNK + (k % ST_GDN_KPS) * (D * 4) + d * 4);
       }
       named_bar(1, ST_NT);
       const float tq = X.red[0] + X.red[1] + X.red[2] + X.red[3];
@@ -621,15 +718,15 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
         ks[tid] = kv * k_scale;
       }
       named_bar(1, ST_NT);
-      const float decay = expf(__ldcg(a.g + h));
-      const float beta = bf2f(__ldcg(a.beta + h));
+      const float decay = expf(gval);
+      const float beta = bval;
       float pred = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) pred += s[i] * decay * ks[kg * 64 + i];
       red2[kg * D + d] = pred;
       named_bar(1, ST_NT);
       const float ptot = red2[d] + red2[D + d];
-      const float delta = (bf2f(__ldcg(a.v + (size_t)h * D + d)) - ptot) * beta;
+      const float delta = (vval - ptot) * beta;
       named_bar(1, ST_NT);  // red2 is read before it is reused
       float o = 0.f;
       float* Sg = a.state + (size_t)h * D * D;
@@ -654,8 +751,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
           named_bar(2, D);
           const float var = (wsum[0] + wsum[1] + wsum[2] + wsum[3]) / (float)D;
           const bf16 normed = f2bf(c * rsqrtf(var + a.eps));
-          const bf16 tv = f2bf(bf2f(normed) * bf2f(a.norm_w[d]));
-          const float zv = bf2f(__ldcg(a.z + (size_t)h * D + d));
+          const bf16 tv = f2bf(bf2f(normed) * nwv);
           const bf16 zs = f2bf(zv / (1.0f + expf(-zv)));
           *out = f2bf(bf2f(tv) * bf2f(zs));
         }
@@ -668,45 +764,20 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
   }
 }
 
-// Attention units on the consumer warps, each over ST_ATTN_SLOTS contiguous
-// ring slots of scratch (aligned so they never wrap the ring).  Two positions
-// per warp in flight and the queries read from shared memory keep the unit
-// inside this kernel's register budget (9 warps: 168 registers a thread); each
-// head layout is a separate (not inlined) function with its own allocation.
-template <int D, int G>
-__device__ __noinline__ void st_attn_unit(const AttnArgs& a, int kh, int split, float* scratch, int* s_last) {
-  attn_unit<D, G, 2, false>(a, kh, split, scratch, s_last);
-}
-
-__device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32_t& n) {
-  const int tid = threadIdx.x;
+// Attention units on the consumer warps, in a scratch region of their own
+// (the KV rows are read directly, not streamed through the ring).  The step
+// kernel carries the Qwen3.5 layout only (head dim 256, four query heads per
+// KV head): two positions per warp in flight and the queries read from
+// shared memory keep the unit inside this kernel's register budget (9 warps:
+// 168 registers a thread); other layouts use the per-launch attention kernel.
+__device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X) {
   int u0, u1;
   st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
   for (int u = u0; u < u1; ++u) {
-    const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
-    if (tid == 0) {
-      int ok = 1;
-      for (int i = 0; i < cnt && ok; ++i) {
-        const uint32_t m = n + i;
-        if (!st_mbar_wait(X.full0 + 8 * (m % ST_SLOTS), (m / ST_SLOTS) & 1u, X.abort_flag)) ok = 0;
-      }
-      *X.flag = ok;
-    }
+    const int kh = u / S.attn.nsplit, split = u - kh * S.attn.nsplit;
+    int* s_last = X.flag + 1;
+    attn_unit<256, 4, 2, false>(S.attn, kh, split, X.attn, s_last);
     named_bar(1, ST_NT);
-    if (*X.flag) {
-      float* scratch = reinterpret_cast<float*>(X.ring + ((n + cnt - ST_ATTN_SLOTS) % ST_SLOTS) * ST_CHUNK);
-      const int kh = u / S.attn.nsplit, split = u - kh * S.attn.nsplit;
-      int* s_last = X.flag + 1;
-#define QWEN_ST_ATTN(DD, GG) \
-  if (S.attn_dim == DD && S.attn_g == GG) st_attn_unit<DD, GG>(S.attn, kh, split, scratch, s_last);
-      QWEN_ST_ATTN(256, 1) else QWEN_ST_ATTN(256, 2) else QWEN_ST_ATTN(256, 4)
-      else QWEN_ST_ATTN(128, 1) else QWEN_ST_ATTN(128, 2) else QWEN_ST_ATTN(128, 4) else QWEN_ST_ATTN(128, 8)
-#undef QWEN_ST_ATTN
-    }
-    named_bar(1, ST_NT);
-    if (tid == 0)
-      for (int i = 0; i < cnt; ++i) mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
-    n += cnt;
   }
 }
 
@@ -722,9 +793,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   X.red = reinterpret_cast<float*>(st_smem + StSmem::red);
   X.misc = reinterpret_cast<unsigned long long*>(st_smem + StSmem::misc);
   X.flag = reinterpret_cast<int*>(X.misc + 16);
+  X.attn = reinterpret_cast<float*>(st_smem + StSmem::attn);
   X.full0 = sbase + StSmem::bars;
   X.empty0 = X.full0 + 8 * ST_SLOTS;
   X.abort_flag = P.abort_flag;
+  X.timeline = P.timeline;
+  X.stage = 0;
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST_SLOTS; ++i) {
       mbar_init(X.full0 + 8 * i, 1);
@@ -744,20 +818,20 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     const StStage& S = P.stages[s];
     if (tid == 0) st_stamp(P, s, ST_TL_WAIT);
     if (s > 0) {
-      if (tid == 0) *X.flag = st_wait_count(P.counters + s - 1, gridDim.x, P.abort_flag) ? 1 : 0;
-      named_bar(1, ST_NT);
-      alive = *X.flag != 0;
-      named_bar(1, ST_NT);
+      bool ok = true;
+      if (tid == 0) ok = st_wait_count(P.counters + s - 1, gridDim.x, P.abort_flag);
+      alive = named_bar_and(1, ST_NT, ok);
       if (!alive) break;
     }
     if (tid == 0) st_stamp(P, s, ST_TL_START);
+    X.stage = s;
     const int kind = S.kind;
     if (kind == ST_GEMV) {
       st_gemv(S, X, n);
     } else if (kind == ST_GDN) {
       st_gdn(S, X, n);
     } else {
-      st_attn(S, X, n);
+      st_attn(S, X);
     }
     named_bar(1, ST_NT);
     if (tid == 0) {
@@ -780,11 +854,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
 }
 
 // ---------------------------------------------------------------------------
-// Weight packing: [N, K] E4M3 row-major + block scales -> chunks of 16 rows x
-// 512 K.  Chunk (t, c) holds, for group j = 0..7 (64 K each) and half
-// h = 0, 1, the 512 bytes lane*16 + i = W[16t + 8h + lane/4][512c + 64j +
-// 16(lane%4) + i], then the FP32 scales of its four 128-K blocks (row block
-// 16t / 128).  Rows past N are zero.  One thread per 16 bytes.
+// Weight packing: [N, K] E4M3 row-major + block scales -> chunks of 32 rows x
+// 512 K.  Chunk (t, c) holds, for row group rg = 0, 1, group j = 0..7 (64 K
+// each) and half h = 0, 1, the 512 bytes lane*16 + i = W[32t + 16rg + 8h +
+// lane/4][512c + 64j + 16(lane%4) + i], then the FP32 scales of its four
+// 128-K blocks (row block 32t / 128).  Rows past N are zero.  One thread per
+// 16 bytes.
 // ---------------------------------------------------------------------------
 template <typename ST>
 __global__ void step_pack_kernel(const uint8_t* __restrict__ w, const void* __restrict__ s, int N, int K, int kblk,
@@ -799,8 +874,8 @@ __global__ void step_pack_kernel(const uint8_t* __restrict__ w, const void* __re
     const int t = (int)(chunk / C), c = (int)(chunk - (long long)t * C);
     uint8_t* dst = out + chunk * ST_CHUNK;
     if (p < ST_WBYTES / 16) {
-      const int j = p >> 6, h = (p >> 5) & 1, lane = p & 31;
-      const int row = t * ST_ROWS + 8 * h + (lane >> 2);
+      const int rg = p >> 9, j = (p >> 6) & 7, h = (p >> 5) & 1, lane = p & 31;
+      const int row = t * ST_ROWS + 16 * rg + 8 * h + (lane >> 2);
       const int k = c * ST_KC + 64 * j + 16 * (lane & 3);
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (row < N) v = *reinterpret_cast<const uint4*>(w + (size_t)row * K + k);

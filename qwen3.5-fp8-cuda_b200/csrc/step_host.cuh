@@ -72,7 +72,7 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
       return cudaErrorInvalidValue;
     if (in.pro < QWEN_STEP_PRO_PLAIN || in.pro > QWEN_STEP_PRO_SLICES_NORM) return cudaErrorInvalidValue;
     if (in.pro != QWEN_STEP_PRO_SLICES_NORM && !in.x) return cudaErrorInvalidValue;
-    if (in.pro != QWEN_STEP_PRO_PLAIN && !in.norm_w) return cudaErrorInvalidValue;
+    if (in.pro != QWEN_STEP_PRO_PLAIN && (!in.norm_w || in.K > ST_NORM_MAXK)) return cudaErrorInvalidValue;
     if (in.pro == QWEN_STEP_PRO_EMBED_NORM && (!in.token || in.x_rows <= 0)) return cudaErrorInvalidValue;
     if (in.pro == QWEN_STEP_PRO_SLICES_NORM && (!in.res || !in.sl_in || in.sl_stride < in.K))
       return cudaErrorInvalidValue;
@@ -198,9 +198,7 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     const int G = in.a_heads / in.a_kv;
     const int smem = 4 * (G * in.a_dim + ATTN_WARPS * G * in.a_dim + 2 * ATTN_WARPS * G + 2 * in.a_dim +
                           ATTN_WARPS * in.a_dim);
-    if (!((in.a_dim == 256 && (G == 1 || G == 2 || G == 4)) || (in.a_dim == 128 && (G == 1 || G == 2 || G == 4 || G == 8))) ||
-        smem > ST_ATTN_SLOTS * ST_CHUNK)
-      return cudaErrorInvalidValue;
+    if (in.a_dim != 256 || G != 4 || smem > ST_ATTN_SMEM) return cudaErrorNotSupported;
     AttnArgs& a = o.attn;
     a = AttnArgs{};
     a.q = static_cast<const bf16*>(in.a_q);

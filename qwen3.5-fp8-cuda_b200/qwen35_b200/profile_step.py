@@ -15,7 +15,12 @@ name, where the step's time goes:
   starting this stage (the cost of the grid-wide dependency);
 * ``work``: median and max over CTAs of the stage's own work;
 * ``lead``: how far ahead of the stage's start the median producer had
-  issued the stage's last item (negative: the stream was behind).
+  issued the stage's last item (negative: the stream was behind);
+* ``pblk`` / ``cblk``: median ns the producer was blocked on a full ring while
+  issuing the stage / consumer warp 0 was blocked on copies not yet landed
+  (a producer blocked means the consumers set the pace; consumers blocked
+  means the stream does);
+* ``pro``: median time from the stage's start to its x prologue being done.
 
 Also prints the step time measured with CUDA events over ``--steps`` steps.
 """
@@ -29,6 +34,7 @@ import statistics
 import torch
 
 KINDS = {0: "gemv", 1: "gdn", 2: "attn"}
+NF = 8  # timeline words per (stage, CTA)
 
 
 def stage_names(cfg):
@@ -42,16 +48,18 @@ def stage_names(cfg):
 
 
 def timeline(eng):
-    """One step with the timeline on: [stages, grid, 5] int64 ns from the earliest stamp."""
+    """One step with the timeline on: [stages, grid, 8] int64 (stamps in ns from the earliest one)."""
     ns, grid = len(eng.stages), eng.grid
-    buf = torch.zeros(ns * grid * 5, dtype=torch.int32, device=eng.device)
+    buf = torch.zeros(ns * grid * NF, dtype=torch.int32, device=eng.device)
     eng.lib.qwen_step_set_timeline(eng.prog, ctypes.c_void_p(buf.data_ptr()))
     eng.step()
     torch.cuda.synchronize(eng.device)
     eng.lib.qwen_step_set_timeline(eng.prog, ctypes.c_void_p(0))
-    t = (buf.cpu().to(torch.int64) & 0xFFFFFFFF).view(ns, grid, 5)
+    t = (buf.cpu().to(torch.int64) & 0xFFFFFFFF).view(ns, grid, NF)
     base = int(t[0, :, 0].min())
-    return (t - base) % (1 << 32)
+    t[:, :, :5] = (t[:, :, :5] - base) % (1 << 32)
+    t[:, :, 7] = (t[:, :, 7] - base) % (1 << 32)
+    return t
 
 
 def summarize(cfg, t):
@@ -64,7 +72,9 @@ def summarize(cfg, t):
         work = (end - start).tolist()
         rows.append(dict(stage=s, name=names[s] if s < len(names) else str(s), span=last_end - prev_end,
                          sync=int(start.median()) - prev_end, work_med=statistics.median(work), work_max=max(work),
-                         lead=int(start.median()) - int(p1.median())))
+                         lead=int(start.median()) - int(p1.median()),
+                         pblk=int(t[s, :, 5].median()), cblk=int(t[s, :, 6].median()),
+                         pro=max(0, int((t[s, :, 7] - start).median())) if int(t[s, :, 7].max()) else 0))
         prev_end = last_end
     return rows
 
@@ -75,16 +85,17 @@ def report(cfg, t, per_stage=False, out=print):
     out(f"timeline step: {total / 1000:.1f} us")
     agg = {}
     for r in rows:
-        a = agg.setdefault(r["name"], dict(n=0, span=0, sync=0, work_med=0, work_max=0, lead=0))
+        a = agg.setdefault(r["name"], dict(n=0, span=0, sync=0, work_med=0, work_max=0, lead=0, pblk=0, cblk=0, pro=0))
         a["n"] += 1
-        for k in ("span", "sync", "work_med", "work_max", "lead"):
+        for k in ("span", "sync", "work_med", "work_max", "lead", "pblk", "cblk", "pro"):
             a[k] += r[k]
     out(f"{'stage':10s} {'n':>4s} {'span us':>9s} {'share':>6s} {'sync us':>8s} {'work med':>9s} {'work max':>9s} "
-        f"{'lead us':>8s}  (per-stage means)")
+        f"{'lead us':>8s} {'pblk us':>8s} {'cblk us':>8s} {'pro us':>7s}  (per-stage means)")
     for name, a in agg.items():
         n = a["n"]
         out(f"{name:10s} {n:4d} {a['span'] / n / 1000:9.2f} {a['span'] / total:6.1%} {a['sync'] / n / 1000:8.2f} "
-            f"{a['work_med'] / n / 1000:9.2f} {a['work_max'] / n / 1000:9.2f} {a['lead'] / n / 1000:8.2f}")
+            f"{a['work_med'] / n / 1000:9.2f} {a['work_max'] / n / 1000:9.2f} {a['lead'] / n / 1000:8.2f} "
+            f"{a['pblk'] / n / 1000:8.2f} {a['cblk'] / n / 1000:8.2f} {a['pro'] / n / 1000:7.2f}")
     if per_stage:
         for r in rows:
             out(str(r))

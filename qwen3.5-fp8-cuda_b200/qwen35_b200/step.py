@@ -102,10 +102,14 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
     residual projections (default: chosen by the library).
     """
 
+    # Fewest positions per attention split: short splits keep a unit's chain
+    # of KV-row round trips short (all splits run at once, one per CTA).
+    ATTN_CHUNK = 8
+
     def __init__(self, cfg, weights, max_seq: int = 4096, device="cuda", keep_logits: bool = False,
                  attn_chunk: int | None = None, nslice: int = 0):
         super().__init__(cfg, weights, max_seq=max_seq, device=device, keep_logits=keep_logits,
-                         attn_chunk=attn_chunk, slices=True)
+                         attn_chunk=self.ATTN_CHUNK if attn_chunk is None else attn_chunk, slices=True)
         self.nslice = int(nslice)
         self.packed = {}
         self._pack_all()

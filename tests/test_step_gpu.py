@@ -35,22 +35,23 @@ def st():
 def unpack(packed: torch.Tensor, n: int, k: int):
     """Inverse of the documented chunk layout: (weights [n, k] u8, scales [tiles][C][4])."""
     c = k // 512
-    tiles = (n + 15) // 16
-    raw = packed.cpu().view(tiles, c, 8208)
-    wb = raw[:, :, :8192].reshape(tiles, c, 8, 2, 32, 16)  # [t][c][j][h][lane][byte]
-    w = torch.zeros(tiles * 16, k, dtype=torch.uint8)
-    for h in range(2):
-        for lane in range(32):
-            rows = torch.arange(tiles) * 16 + 8 * h + lane // 4
-            for j in range(8):
-                for cc in range(c):
-                    k0 = cc * 512 + 64 * j + 16 * (lane % 4)
-                    w[rows, k0:k0 + 16] = wb[:, cc, j, h, lane]
-    scales = raw[:, :, 8192:].contiguous().view(F32).reshape(tiles, c, 4)
+    tiles = (n + 31) // 32
+    raw = packed.cpu().view(tiles, c, 16400)
+    wb = raw[:, :, :16384].reshape(tiles, c, 2, 8, 2, 32, 16)  # [t][c][rg][j][h][lane][byte]
+    w = torch.zeros(tiles * 32, k, dtype=torch.uint8)
+    for rg in range(2):
+        for h in range(2):
+            for lane in range(32):
+                rows = torch.arange(tiles) * 32 + 16 * rg + 8 * h + lane // 4
+                for j in range(8):
+                    for cc in range(c):
+                        k0 = cc * 512 + 64 * j + 16 * (lane % 4)
+                        w[rows, k0:k0 + 16] = wb[:, cc, rg, j, h, lane]
+    scales = raw[:, :, 16384:].contiguous().view(F32).reshape(tiles, c, 4)
     return w[:n], scales
 
 
-@pytest.mark.parametrize("n,k,f32", [(40, 1024, False), (256, 2560, True)])
+@pytest.mark.parametrize("n,k,f32", [(40, 1024, False), (4, 512, False), (256, 2560, True)])
 def test_pack_layout(st, n, k, f32):
     _, step = st
     g = synth.gen(n + k)
@@ -60,8 +61,8 @@ def test_pack_layout(st, n, k, f32):
     torch.cuda.synchronize()
     wu, sc = unpack(packed, n, k)
     assert torch.equal(wu, w)
-    for t in range((n + 15) // 16):
-        rb = (16 * t) // 128
+    for t in range((n + 31) // 32):
+        rb = (32 * t) // 128
         assert torch.equal(sc[t].reshape(-1), s[rb].float())
 
 
