@@ -1,33 +1,42 @@
 #!/usr/bin/env python
 """Batch-1 greedy decode throughput of the random-init Qwen3.5-4B text decoder
-on B200, plus the HBM roofline of the dominant GEMV kernel.
+on B200, plus the HBM roofline of the dominant kernel.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--engine step|launch]
 
-One step = one decode token through the whole 32-layer model (162 kernels in
-one CUDA graph).  Timing: a 128-token seeded prompt is fed first, then W
-untimed decode steps, then EXACTLY K steps bracketed by a barrier and
+One step = one decode token through the whole 32-layer model.  On one GPU the
+default engine runs the token as one launch of the persistent step kernel
+(qwen35_b200.step); ``--engine launch`` runs the per-stage launch chain (162
+kernels in one CUDA graph), which is also the tensor-parallel engine's form
+for N > 1.  Timing: a 128-token seeded prompt is fed first, then W untimed
+decode steps, then EXACTLY K steps bracketed by a barrier and
 torch.cuda.synchronize(), timed with CUDA events on the launching stream; the
 max over ranks is reported.  Every step streams ~4.3 GB of weights, far more
 than the 126 MB L2, so no flush is needed between steps.
 
 Keys beyond the base contract:
-  e2e           the same K steps through the public API Qwen35DecodeEngine.decode()
-                (token in from pinned memory, graph replay, next token and a
-                sequence number written to pinned memory, host polls)
-  roofline      the dominant kernel (gemv_tcw_kernel, the tcgen05 + TMA GEMV with
-                the weights as the N = 256 MMA operand and the fused greedy
-                argmax) timed alone on the LM-head launch of config 2, back to
-                back (burst peak)
+  e2e           the same K steps through the public API engine.decode() (token
+                in from pinned memory, the step, next token and a sequence
+                number written to pinned memory, host polls)
+  roofline      the dominant kernel: the step kernel (one launch per token, all
+                of the step's bytes) with the launch engine, the dominant GEMV
+                kernel on the LM-head launch of config 2
   step_roofline algorithmic bytes of a whole decode step / device time per step
+  stage_roofline (step kernel) per stage kind, from the kernel's own timeline
+                (qwen35_b200.profile_step): bytes of the stage / its span on the
+                critical path, and the span's share of the step
+  lm_head_kernel the LM-head GEMV + argmax kernel of the launch engine timed alone
   gemv_shapes   (1 GPU) every config 0/1 decode GEMV shape timed alone, through the
                 reference entry point and PDL-chained (qwen35_b200.profile_gemv)
   cpu_baseline  the CPU oracle port (explicit FP8->FP32 dequant + torch matmul)
-                on a bounded sample of the step, scaled to tok/s
+                on a bounded sample of the step, scaled to tok/s, with the
+                dequant and the matmul of every decode GEMV shape timed apart
   clocks        nvidia-smi samples taken during the timed region
 
 --impl reference times the reference's path on the host CPU cores (the oracle
-port; the reference has no CPU implementation of its own), rank 0 only.
+port; the reference has no CPU implementation of its own), rank 0 only; its
+line also carries the reference's own GEMV kernel (built from its sources into
+oracle/_ref) timed per decode shape on the GPU, when that build is present.
 """
 
 from __future__ import annotations
@@ -63,6 +72,8 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="disable programmatic dependent launch")
+    ap.add_argument("--engine", choices=["step", "launch"], default="step",
+                    help="one GPU: persistent step kernel (default) or the per-stage launch chain")
     return ap.parse_args()
 
 
@@ -75,9 +86,10 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def load_traffic():
-    """DRAM bytes per LM-head launch from the committed ncu summary, if any."""
-    path = os.path.join(REPO, "profiles", "gemv_lm_head_config2_ncu.txt")
+def load_traffic(name="gemv_lm_head_config2_ncu.txt"):
+    """DRAM bytes per launch from a committed ncu summary under profiles/ (the
+    line ``dram_bytes_per_launch = ...``), if any."""
+    path = os.path.join(REPO, "profiles", name)
     if not os.path.exists(path):
         return None
     with open(path) as f:
@@ -85,6 +97,30 @@ def load_traffic():
             if line.startswith("dram_bytes_per_launch"):
                 return int(float(line.split("=")[1].split()[0]))
     return None
+
+
+def stage_bytes(cfg, w):
+    """Algorithmic bytes per stage name of the step kernel's program (weights
+    and scales of the stage's GEMVs, the GatedDeltaNet state read + write),
+    summed over the step."""
+    out = {}
+
+    def add(name, *mats):
+        out[name] = out.get(name, 0) + sum(tensor_bytes(m) for m in mats)
+
+    for i, ly in enumerate(w["layers"]):
+        if cfg.layer_types[i] == "full_attention":
+            add("qkv", ly["q_proj"], ly["k_proj"], ly["v_proj"])
+            add("o_proj", ly["o_proj"])
+        else:
+            add("in_proj", ly["in_proj_qkv"], ly["in_proj_z"], ly["in_proj_a"], ly["in_proj_b"])
+            out["gdn"] = out.get("gdn", 0) + 2 * cfg.linear_num_value_heads * cfg.linear_key_head_dim * \
+                cfg.linear_value_head_dim * 4
+            add("out_proj", ly["out_proj"])
+        add("gate_up", ly["gate_proj"], ly["up_proj"])
+        add("down", ly["down_proj"])
+    add("lm_head", w["lm_head"])
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -195,9 +231,14 @@ def lm_head_bytes(cfg, w) -> int:
 # ---------------------------------------------------------------------------
 # CPU oracle leg
 # ---------------------------------------------------------------------------
+UNIT_KINDS = ("linear_attention", "full_attention", "head")
+
+
 def time_cpu_units(cfg, layers, head, n_units, warmup_units=1):
-    """Run `n_units` decode-step units of the CPU oracle (layer i mod 33, the
-    33rd unit being the LM head) and return seconds per unit list."""
+    """Run `n_units` decode-step units of the CPU oracle, cycling through a
+    GatedDeltaNet layer, a full-attention layer and the LM head (so every
+    kind of unit of a token is in every sample of three or more units);
+    returns [(kind, seconds)] of the timed units."""
     from oracle import ops
     from oracle.model import OracleModel
 
@@ -209,11 +250,10 @@ def time_cpu_units(cfg, layers, head, n_units, warmup_units=1):
     hidden = (torch.randn(cfg.hidden_size, generator=torch.Generator().manual_seed(1)) * 0.5).to(torch.bfloat16)
     times = []
     for u in range(n_units + warmup_units):
-        idx = u % (cfg.num_hidden_layers + 1)
+        kind = UNIT_KINDS[u % 3]
         t0 = time.perf_counter()
-        if idx < cfg.num_hidden_layers:
-            lt = cfg.layer_types[idx]
-            li = 0 if lt == "linear_attention" else 1
+        if kind != "head":
+            li = 0 if kind == "linear_attention" else 1
             ly = wd["layers"][li]
             res = hidden
             h = ops.rmsnorm(hidden, ly["input_layernorm"])
@@ -227,7 +267,7 @@ def time_cpu_units(cfg, layers, head, n_units, warmup_units=1):
             ops.argmax_first(logits)
         dt = time.perf_counter() - t0
         if u >= warmup_units:
-            times.append((idx, dt))
+            times.append((kind, dt))
     return times
 
 
@@ -265,39 +305,100 @@ def cpu_sample_weights(cfg, seed=7):
 
 
 def cpu_tok_per_s(cfg, times):
-    """Scale per-unit times to one full decode step (32 layers + head)."""
-    per_idx = {}
-    for idx, dt in times:
-        per_idx.setdefault(idx, []).append(dt)
-    lin = [d for i, ds in per_idx.items() if i < cfg.num_hidden_layers and cfg.layer_types[i] == "linear_attention"
-           for d in ds]
-    full = [d for i, ds in per_idx.items() if i < cfg.num_hidden_layers and cfg.layer_types[i] == "full_attention"
-            for d in ds]
-    head = per_idx.get(cfg.num_hidden_layers, [])
+    """Scale per-unit medians to one full decode step (24 GDN + 8 full layers + head)."""
+    per = {k: [dt for kind, dt in times if kind == k] for k in UNIT_KINDS}
+    t_lin = statistics.median(per["linear_attention"]) if per["linear_attention"] else 0.0
+    t_full = statistics.median(per["full_attention"]) if per["full_attention"] else t_lin
+    t_head = statistics.median(per["head"]) if per["head"] else 0.0
     n_lin = cfg.layer_types.count("linear_attention")
     n_full = cfg.num_hidden_layers - n_lin
-    t_lin = statistics.median(lin) if lin else 0.0
-    t_full = statistics.median(full) if full else t_lin
-    t_head = statistics.median(head) if head else 0.0
     step = n_lin * t_lin + n_full * t_full + t_head
     return 1.0 / step, step
 
 
-def run_cpu_baseline(cfg, n_units=34):
+def decode_gemv_shapes(cfg):
+    """[(N, K, launches per token)] of every linear weight of one decode step."""
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    n_lin = cfg.layer_types.count("linear_attention")
+    n_full = cfg.num_hidden_layers - n_lin
+    qd = cfg.num_attention_heads * cfg.head_dim
+    kvd = cfg.num_key_value_heads * cfg.head_dim
+    nv = cfg.linear_num_value_heads
+    return [(I, H, 2 * cfg.num_hidden_layers), (H, I, cfg.num_hidden_layers),
+            (2 * qd, H, n_full), (kvd, H, 2 * n_full), (H, qd, n_full),
+            (cfg.conv_dim, H, n_lin), (cfg.linear_value_dim, H, n_lin), (nv, H, 2 * n_lin),
+            (H, cfg.linear_value_dim, n_lin), (cfg.vocab_size, H, 1)]
+
+
+def cpu_gemv_split(cfg, runs=10):
+    """The reference path's two host costs per token, timed apart: the
+    explicit FP8 -> FP32 block dequantisation (main.py:497-501) and the FP32
+    matmul, each the median of `runs` runs per decode GEMV shape, summed over
+    the shapes' launches per token."""
+    from oracle import ops, synth
+    g = synth.gen(11)
+    dq_total = mm_total = 0.0
+    rows = []
+    for n, k, count in decode_gemv_shapes(cfg):
+        w, s32 = synth.fp8_weight(n, k, g)
+        s = s32.to(torch.bfloat16)
+        x = synth.bf16_vector(k, g).float()
+        t_dq, t_mm = [], []
+        for _ in range(runs):
+            t0 = time.perf_counter()
+            wd = ops.dequant(w, s)
+            t1 = time.perf_counter()
+            (wd @ x).to(torch.bfloat16)
+            t2 = time.perf_counter()
+            t_dq.append(t1 - t0)
+            t_mm.append(t2 - t1)
+        dq, mm = statistics.median(t_dq), statistics.median(t_mm)
+        dq_total += count * dq
+        mm_total += count * mm
+        rows.append({"shape": f"{n}x{k}", "per_token": count, "dequant_ms": round(dq * 1e3, 3),
+                     "matmul_ms": round(mm * 1e3, 3)})
+        del w, wd
+    return {"dequant_s_per_token": round(dq_total, 4), "matmul_s_per_token": round(mm_total, 4),
+            "sum_s_per_token": round(dq_total + mm_total, 4), "runs_per_shape": runs,
+            "statistic": "median", "shapes": rows}
+
+
+def run_cpu_baseline(cfg, n_units=33):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     layers, head = cpu_sample_weights(cfg)
     times = time_cpu_units(cfg, layers, head, n_units)
     tps, step_s = cpu_tok_per_s(cfg, times)
-    return {"value": round(tps, 6), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n_units} units of one decode step (GDN / full-attention layers at 4B shapes and the "
-                      f"248320x2560 LM head, explicit FP8->FP32 dequant + torch matmul), median per unit type, "
-                      f"scaled to 24 GDN + 8 full layers + head = {step_s:.3f} s/token"}
+    out = {"value": round(tps, 6), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+           "sample": f"{n_units} units of one decode step cycling GDN layer / full-attention layer / LM head at "
+                     f"4B shapes (explicit FP8->FP32 dequant + torch matmul), median per unit kind, scaled to "
+                     f"24 GDN + 8 full layers + head = {step_s:.3f} s/token"}
+    try:
+        out["gemv_split"] = cpu_gemv_split(cfg)
+    except Exception as exc:  # reported, never allowed to drop the baseline
+        out["gemv_split"] = {"error": repr(exc)[:200]}
+    return out
 
 
 # ---------------------------------------------------------------------------
 # Reference arm: the reference's path on the host CPU (oracle port)
 # ---------------------------------------------------------------------------
+def ref_gpu_gemv_shapes(peak):
+    """The reference's own GEMV kernel (launch_gemv_v4_extern of
+    fused_kernels.cu:1328-1336, built unmodified for sm_100a into oracle/_ref)
+    timed per config 0/1 decode shape on this GPU, by the same method as the
+    gemv_shapes leg of our arm; None when that build or a GPU is absent."""
+    path = os.path.join(REPO, "oracle", "_ref", "libref_fused.so")
+    if not (os.path.exists(path) and torch.cuda.is_available()):
+        return None
+    import ctypes
+    from qwen35_b200.profile_gemv import time_shapes
+    ref = ctypes.CDLL(path)
+    ref.launch_gemv_v4_extern.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+    ref.launch_gemv_v4_extern.restype = None
+    return time_shapes(peak, ref_lib=ref, chained=False)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -306,21 +407,31 @@ def run_reference(args):
     cfg = qwen35_4b()
     torch.set_num_threads(os.cpu_count() or 1)
     layers, head = cpu_sample_weights(cfg)
-    # each step is one unit (one layer or the LM head) of the decode step
-    times = time_cpu_units(cfg, layers, head, args.steps, warmup_units=args.warmup)
+    # each step is one unit of a decode token, cycling GDN layer / full-attention
+    # layer / LM head, so every kind is timed whatever K is (K >= 3)
+    times = time_cpu_units(cfg, layers, head, max(3, args.steps), warmup_units=args.warmup)
     tps, step_s = cpu_tok_per_s(cfg, times)
-    total = sum(dt for _, dt in times)
     line = {
         "metric": METRIC, "value": round(tps, 6), "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / max(1, len(times)), 3),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * step_s, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_block(args),
         "cpu_baseline": {"value": round(tps, 6), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"{args.steps} timed units, each one layer (GDN or full attention, 4B shapes) "
-                                   f"or the LM head of a decode step, explicit FP8->FP32 dequant + torch matmul; "
-                                   f"scaled to one token = {step_s:.3f} s"},
+                         "sample": f"{len(times)} timed units cycling GDN layer / full-attention layer / LM head "
+                                   f"(4B shapes), explicit FP8->FP32 dequant + torch matmul; medians per kind "
+                                   f"scaled to one token (24 GDN + 8 full + head) = {step_s:.3f} s"},
         "e2e": {"value": round(tps, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    try:
+        peak, _ = load_peaks()
+        rows = ref_gpu_gemv_shapes(peak)
+        if rows is not None:
+            line["ref_gpu_gemv_shapes"] = {
+                "kernel": "reference gemv_v4_kernel via launch_gemv_v4_extern (oracle/_ref, sm_100a build of "
+                          "fused_kernels.cu)", "unit": "us per launch; GB/s of algorithmic bytes",
+                "rows": rows}
+    except Exception as exc:  # context only, never allowed to drop the line
+        line["ref_gpu_gemv_shapes"] = {"error": repr(exc)[:200]}
     print(json.dumps(line), flush=True)
 
 
@@ -361,6 +472,7 @@ def run_ours(args):
     from qwen35_b200 import _lib
     from qwen35_b200.config import qwen35_4b
     from qwen35_b200.engine import Qwen35DecodeEngine
+    from qwen35_b200.step import Qwen35StepEngine
     from qwen35_b200.tp import Qwen35TPDecodeEngine
     from qwen35_b200.weights import random_weights
 
@@ -375,8 +487,11 @@ def run_ours(args):
         eng = Qwen35TPDecodeEngine(cfg, w, rank, world, max_seq=max_seq)
         del w
         torch.cuda.empty_cache()
+    elif args.engine == "step":
+        eng = Qwen35StepEngine(cfg, w, max_seq=max_seq)
     else:
         eng = Qwen35DecodeEngine(cfg, w, max_seq=max_seq)
+    step_engine = isinstance(eng, Qwen35StepEngine)
     eng.capture()
     g = torch.Generator().manual_seed(1000 + args.seed)
     prompt = torch.randint(0, cfg.vocab_size, (PROMPT_LEN,), generator=g).tolist()
@@ -417,8 +532,8 @@ def run_ours(args):
     clocks = sampler.stop()
     assert _lib.device_error() == 0, "device error word set (bounded wait timed out)"
 
-    # dominant kernel alone: the LM-head streaming GEMV (config 2 launch; this
-    # rank's vocabulary shard under tensor parallelism)
+    # the launch engine's LM-head streaming GEMV + argmax kernel alone (config 2
+    # launch; this rank's vocabulary shard under tensor parallelism)
     wh, sh = eng.w["lm_head"]
     row_offset = eng.w.get("lm_row_offset", 0)
     ws = torch.zeros(2, dtype=torch.int64, device="cuda")
@@ -448,9 +563,25 @@ def run_ours(args):
     head_s = h0.elapsed_time(h1) / 1000.0 / reps
     peak, peak_kind = load_peaks()
     hb = wh.numel() + sh.numel() * sh.element_size() + 2 * cfg.hidden_size + 8
-    achieved = hb / head_s / 1e9
+    head_gbs = hb / head_s / 1e9
     sbytes = step_bytes(cfg, eng.w, ctx0 + args.steps // 2, eng.cfg)
     step_s = dev_ms / 1000.0 / args.steps
+    step_gbs = sbytes / step_s / 1e9
+    head_kernel = {"kernel": "gemv_tcw_kernel<bf16,false> (tcgen05 N=256 + TMA) on the LM head "
+                             "(248320x2560 E4M3, config 2)", "achieved": round(head_gbs, 1), "unit": "GB/s",
+                   "frac": round(head_gbs / peak, 4), "bytes_per_launch": hb, "us_per_launch": round(head_s * 1e6, 2),
+                   "traffic": load_traffic()}
+    if step_engine:
+        # the dominant (only) kernel of a step: the persistent step kernel; one
+        # launch per step, so its launch time is the device time per step
+        roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(step_gbs / peak, 4), "traffic": load_traffic("step_kernel_config3_ncu.txt"),
+                    "kernel": "step_kernel (persistent, one cooperative launch per token: every GEMV, GatedDeltaNet, "
+                              "attention and LM-head stage)",
+                    "bytes_per_launch": sbytes, "us_per_launch": round(step_s * 1e6, 2), "peak_kind": peak_kind}
+    else:
+        roofline = {"bound": "hbm", **{k: v for k, v in head_kernel.items() if k != "kernel"}, "peak": peak,
+                    "peak_kind": peak_kind, "kernel": head_kernel["kernel"]}
 
     line = {
         "metric": METRIC,
@@ -465,19 +596,39 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "e4m3xbf16->f32",
         "data": "synthetic (seeded random-init weights and prompt ids)",
-        "config": config_block(args),
+        "config": {**config_block(args), "engine": "step" if step_engine else "launch"},
         "e2e": {"value": round(args.steps / (e2e_ms / 1000.0), 3), "unit": UNIT,
                 "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
         "gpu_launches": eng.kernels_per_step * args.steps,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": load_traffic(),
-                     "kernel": "gemv_tcw_kernel<bf16,false> (tcgen05 N=256 + TMA) on the LM head (248320x2560 E4M3, config 2)",
-                     "bytes_per_launch": hb, "us_per_launch": round(head_s * 1e6, 2), "peak_kind": peak_kind},
-        "step_roofline": {"bytes_per_step": sbytes, "achieved": round(sbytes / step_s / 1e9, 1),
-                          "frac": round(sbytes / step_s / 1e9 / peak, 4), "unit": "GB/s"},
+        "roofline": roofline,
+        "step_roofline": {"bytes_per_step": sbytes, "achieved": round(step_gbs, 1),
+                          "frac": round(step_gbs / peak, 4), "unit": "GB/s"},
+        "lm_head_kernel": head_kernel,
         "clocks": clocks,
         "pdl": not args.no_pdl,
     }
+    if step_engine:
+        try:
+            from qwen35_b200 import profile_step
+            rows = profile_step.summarize(cfg, profile_step.timeline(eng))
+            sb = stage_bytes(cfg, eng.w)
+            agg = {}
+            for r in rows:
+                a = agg.setdefault(r["name"], {"stages": 0, "span_us": 0.0})
+                a["stages"] += 1
+                a["span_us"] += r["span"] / 1000.0
+            total = sum(a["span_us"] for a in agg.values())
+            for name, a in agg.items():
+                b = sb.get(name, 0)
+                a["bytes"] = b
+                a["gbs"] = round(b / (a["span_us"] * 1e3), 1) if a["span_us"] else None
+                a["frac"] = round(a["gbs"] / peak, 4) if a["gbs"] else None
+                a["share"] = round(a["span_us"] / total, 4)
+                a["span_us"] = round(a["span_us"], 1)
+            line["stage_roofline"] = {"unit": "GB/s of the stage's algorithmic bytes over its span on the step's "
+                                              "critical path (one timed step)", "stages": agg}
+        except Exception as exc:  # reported, never allowed to drop the line
+            line["stage_roofline"] = {"error": repr(exc)[:200]}
     if world == 1:
         # every config 0/1 decode GEMV shape alone (after the timed region)
         from qwen35_b200.profile_gemv import time_shapes

@@ -152,13 +152,14 @@ int qwen_step_reset(void* program, cudaStream_t stream);
 
 int qwen_step_destroy(void* program);
 
-/* Profiling: launches record, per stage and CTA, eight words into timeline
- * [nstages][grid][8]: five %globaltimer stamps (low 32 bits, ns) - the
+/* Profiling: launches record, per stage and CTA, ten words into timeline
+ * [nstages][grid][10]: five %globaltimer stamps (low 32 bits, ns) - the
  * consumers' wait for the previous stage begins, ends, their work on the stage
  * ends, the producer issues the stage's first item, has issued its last - then
  * the producer's ns blocked on a full ring while issuing the stage, consumer
- * warp 0's ns blocked on copies not yet landed, and the stamp at which a GEMV
- * stage's x prologue was done.  Null stops it. */
+ * warp 0's ns blocked on copies not yet landed, and for GEMV stages the stamps
+ * at which the x prologue and the last batch's chunk math were done and warp
+ * 0's SM clock cycles inside the chunk math.  Null stops it. */
 int qwen_step_set_timeline(void* program, unsigned* timeline);
 
 /* CTAs a launch uses (one per SM) and its dynamic shared memory in bytes. */

@@ -63,12 +63,15 @@ constexpr int ST_WBYTES = ST_ROWS * ST_KC;     // 16384 weight bytes per chunk
 constexpr int ST_CHUNK = ST_WBYTES + 16;       // + four FP32 block scales
 // Ring of chunk slots.  The bulk-copy engine's rate grows with the size of a
 // copy (measured on B200 through a 128-192 KB ring: 8 KB copies 5.2 TB/s,
-// 16 KB 6.4-6.8, 32 KB 6.9), hence 16 KB chunks.  The slot count is a
-// multiple of the consumer warps: items m and m + ST_SLOTS share a slot and
-// go to the same warp, so no thread ever waits on a phase beyond the next one
-// of a slot's barrier (a parity wait cannot tell those apart).
-constexpr int ST_SLOTS = 8;
+// 16 KB 6.4-6.8, 32 KB 6.9), hence 16 KB chunks.  A chunk is computed by a
+// pair of consumer warps (one 16-row group each), so a slot is held half as
+// long and more of the ring stays in flight.  The slot count is a multiple of
+// the warp pairs: items m and m + ST_SLOTS share a slot and go to the same
+// pair, so no thread ever waits on a phase beyond the next one of a slot's
+// barrier (a parity wait cannot tell those apart).
+constexpr int ST_SLOTS = 12;
 constexpr int ST_CW = 8;                       // consumer warps
+constexpr int ST_PAIRS = ST_CW / 2;            // consumer warp pairs (one chunk each)
 constexpr int ST_NT = ST_CW * 32;
 constexpr int ST_THREADS = ST_NT + 32;         // + the producer warp
 constexpr int ST_MAXK = 9216;                  // longest GEMV input
@@ -77,11 +80,12 @@ constexpr int ST_NORM_MAXK = 3072;             // longest input of a normalising
 constexpr int ST_NORM_MAXB = ST_NORM_MAXK / 128 / ST_CW;
 constexpr int ST_BATCH = 48;                   // chunk partials held before a reduction
 constexpr int ST_MAX_SEG = 4;
-constexpr int ST_ATTN_SMEM = 48 * 1024;       // scratch of an attention unit
+constexpr int ST_ATTN_SLOTS = 3;               // contiguous ring slots of scratch for an attention unit
 constexpr int ST_GDN_D = 128;                  // GatedDeltaNet head dim of the step kernel
 constexpr int ST_GDN_SLOTS = ST_GDN_D * ST_GDN_D * 4 / ST_WBYTES;  // 4: one head's FP32 state
 constexpr int ST_GDN_KPS = ST_WBYTES / (ST_GDN_D * 4);            // 32 key rows of state per slot
-static_assert(ST_SLOTS % ST_CW == 0, "items m and m + ST_SLOTS must go to the same consumer warp");
+static_assert(ST_SLOTS % ST_PAIRS == 0, "items m and m + ST_SLOTS must go to the same consumer warp pair");
+static_assert(ST_SLOTS % ST_ATTN_SLOTS == 0, "attention scratch groups must not wrap the ring");
 static_assert(ST_GDN_SLOTS <= ST_SLOTS, "a head's state must fit the ring");
 static_assert(ST_NT == ATTN_WARPS * 32, "attention units run on the consumer warps");
 
@@ -95,11 +99,9 @@ struct StSmem {
   static constexpr int red = part + ST_BATCH * ST_ROWS * 4;
   static constexpr int misc = red + 64 * 4;
   static constexpr int bars = misc + 32 * 8;
-  static constexpr int attn = (bars + 2 * ST_SLOTS * 8 + 127) / 128 * 128;
-  static constexpr int total = attn + ST_ATTN_SMEM;
+  static constexpr int total = bars + 2 * ST_SLOTS * 8;
 };
-static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8 == 0 && StSmem::attn % 16 == 0,
-              "alignment");
+static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8 == 0, "alignment");
 static_assert(StSmem::total <= 227 * 1024, "shared memory");
 
 struct StStage {
@@ -146,10 +148,11 @@ struct StProgram {
 // item / has issued its last one.
 // Also, in ns: the producer's time blocked on a full ring while issuing the
 // stage, and consumer warp 0's time blocked on copies not yet landed.
-// Last, the stamp at which the stage's x prologue was done (GEMV stages).
+// Then, for GEMV stages: the stamps at which the x prologue was done and the
+// last batch's chunks were, and consumer warp 0's SM cycles inside the chunk math.
 enum : int {
   ST_TL_WAIT = 0, ST_TL_START = 1, ST_TL_END = 2, ST_TL_P0 = 3, ST_TL_P1 = 4, ST_TL_PBLOCK = 5, ST_TL_CBLOCK = 6,
-  ST_TL_PRO = 7, ST_TL = 8
+  ST_TL_PRO = 7, ST_TL_CHUNKS = 8, ST_TL_WCOMP = 9, ST_TL = 10
 };
 __device__ __forceinline__ void st_stamp(const StProgram& P, int s, int field) {
   if (P.timeline) P.timeline[((size_t)s * gridDim.x + blockIdx.x) * ST_TL + field] = (unsigned)globaltimer_ns();
@@ -216,6 +219,9 @@ __device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
 }
 
 // This CTA's contiguous share [u0, u1) of n units.
+__device__ __forceinline__ int st_attn_pad(uint32_t n) {
+  return (int)((ST_ATTN_SLOTS - n % ST_ATTN_SLOTS) % ST_ATTN_SLOTS);
+}
 __device__ __forceinline__ void st_range(int n, int& u0, int& u1) {
   u0 = (int)(((long long)n * blockIdx.x) / gridDim.x);
   u1 = (int)(((long long)n * (blockIdx.x + 1)) / gridDim.x);
@@ -305,7 +311,18 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
           ++n;
         }
       }
-    }  // ST_ATTN: no streamed items (the KV rows are read directly)
+    } else {  // ST_ATTN: scratch slots, no copy (a plain arrival completes the phase)
+      st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
+      for (int u = u0; u < u1 && ok; ++u) {
+        const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
+        for (int i = 0; i < cnt; ++i) {
+          uint32_t slot;
+          if (!(ok = acquire(slot))) break;
+          mbar_arrive(full0 + 8 * slot);
+          ++n;
+        }
+      }
+    }
     st_stamp(P, s, ST_TL_P1);
     st_tl_put(P.timeline, s, ST_TL_PBLOCK, (unsigned)blocked);
   }
@@ -431,24 +448,31 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
     for (int i = 0; i < ST_CW; ++i) tot += red[i];
     rms = rsqrtf(tot / (float)K + S.eps);
   }
+  // normalised values and every block's maximum, the blocks' shuffle
+  // reductions interleaved
+  float mx[MB];
+#pragma unroll
+  for (int i = 0; i < MB; ++i) {
+    if (norm) {
+      const float4 w = wv[i];
+      v[i][0] = bfround(v[i][0] * rms * (1.0f + w.x));
+      v[i][1] = bfround(v[i][1] * rms * (1.0f + w.y));
+      v[i][2] = bfround(v[i][2] * rms * (1.0f + w.z));
+      v[i][3] = bfround(v[i][3] * rms * (1.0f + w.w));
+    }
+    mx[i] = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < MB; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
     const int b = warp + i * ST_CW;
     if (b >= nb) continue;  // warp-uniform
     const int k0 = b * 128 + lane * 4;
-    float x[4];
-    if (norm) {
-      const float4 w = wv[i];
-      x[0] = bfround(v[i][0] * rms * (1.0f + w.x));
-      x[1] = bfround(v[i][1] * rms * (1.0f + w.y));
-      x[2] = bfround(v[i][2] * rms * (1.0f + w.z));
-      x[3] = bfround(v[i][3] * rms * (1.0f + w.w));
-    } else {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) x[q] = v[i][q];
-    }
-    float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-    m = warp_max(m);
+    const float x[4] = {v[i][0], v[i][1], v[i][2], v[i][3]};
+    const float m = mx[i];
     // m = 1.f * 2^(ebits - 127): e = 134 - ebits puts m * 2^e in [2^7, 2^8)
     const int ebits = (int)((__float_as_uint(m) >> 23) & 0xffu);
     int e = m > 0.f ? (ebits == 0 ? 100 : 134 - ebits) : 0;
@@ -469,54 +493,58 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   named_bar(1, ST_NT);
 }
 
-// One chunk (32 rows x 512 K) on one warp: FP32 partial sums of rows
-// 16 rg + g and 16 rg + g + 8 (rg = 0, 1) in acc[2 rg], acc[2 rg + 1], valid
-// in lanes with lane % 4 == 0 (g = lane / 4).
+// FP8 tensor-core MMA D (16x8 f32) = A (16x32 E4M3) x B (32x8 E4M3) (+ C),
+// as plain (non-volatile) asm so the compiler may interleave independent
+// MMAs and hoist the shared-memory loads that feed them.
+__device__ __forceinline__ void st_mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 16-row group (rg) of a chunk (32 rows x 512 K) on one warp: FP32
+// partial sums of rows 16 rg + g and 16 rg + g + 8, valid in lanes with
+// lane % 4 == 0 (g = lane / 4).  All 24 shared loads are issued first; the
+// four 128-K blocks are four independent accumulator chains.
 __device__ __forceinline__ void st_chunk(const uint8_t* base, const uint8_t* xh, const uint8_t* xl, const float* xinv,
-                                         int c, int lane, float (&acc)[4]) {
+                                         int c, int rg, int lane, float& a0, float& a1) {
   const float4 sc = *reinterpret_cast<const float4*>(base + ST_WBYTES);
   const float* xi = xinv + c * 4;
-  const float f[4] = {sc.x * xi[0], sc.y * xi[1], sc.z * xi[2], sc.w * xi[3]};
   // B fragments: lanes 0-3 (column 0) the hi bytes, lanes 4-7 (column 1) the
   // lo bytes of K [512c + 64j + 16(lane % 4), +16) for group j; other columns zero
   uint4 xr[8];
-  if (lane < 8) {
-    const uint8_t* xs = (lane < 4 ? xh : xl) + c * ST_KC + (lane & 3) * 16;
+  const uint8_t* xs = (lane < 4 ? xh : xl) + c * ST_KC + (lane & 3) * 16;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) xr[j] = *reinterpret_cast<const uint4*>(xs + 64 * j);
-  } else {
+  for (int j = 0; j < 8; ++j)
+    xr[j] = lane < 8 ? *reinterpret_cast<const uint4*>(xs + 64 * j) : make_uint4(0u, 0u, 0u, 0u);
+  const uint8_t* wl = base + rg * (ST_WBYTES / 2) + lane * 16;
+  uint4 w0[8], w1[8];  // group j: row g (w0) and row g + 8 (w1)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) xr[j] = make_uint4(0u, 0u, 0u, 0u);
+  for (int j = 0; j < 8; ++j) {
+    w0[j] = *reinterpret_cast<const uint4*>(wl + (2 * j) * 512);
+    w1[j] = *reinterpret_cast<const uint4*>(wl + (2 * j + 1) * 512);
   }
-#pragma unroll 1
-  for (int rg = 0; rg < 2; ++rg) {  // one row group's loads live at a time (register budget)
-    const uint8_t* wl = base + rg * 8192 + lane * 16;
-    float a0 = 0.f, a1 = 0.f;
+  float d[4][4];
+#pragma unroll
+  for (int kb = 0; kb < 4; ++kb) d[kb][0] = d[kb][1] = d[kb][2] = d[kb][3] = 0.f;
+#pragma unroll
+  for (int step = 0; step < 4; ++step)  // MMA `step` of every block's chain
 #pragma unroll
     for (int kb = 0; kb < 4; ++kb) {
-      float d[4];
+      const int j = 2 * kb + (step >> 1);
+      if ((step & 1) == 0)
+        st_mma(d[kb], w0[j].x, w1[j].x, w0[j].y, w1[j].y, xr[j].x, xr[j].y);
+      else
+        st_mma(d[kb], w0[j].z, w1[j].z, w0[j].w, w1[j].w, xr[j].z, xr[j].w);
+    }
+  const float f[4] = {sc.x * xi[0], sc.y * xi[1], sc.z * xi[2], sc.w * xi[3]};
+  a0 = 0.f;
+  a1 = 0.f;
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = 2 * kb + jj;
-        const uint4 r0 = *reinterpret_cast<const uint4*>(wl + (2 * j) * 512);      // row g
-        const uint4 r1 = *reinterpret_cast<const uint4*>(wl + (2 * j + 1) * 512);  // row g + 8
-        if (jj == 0) {
-          mma_e4m3_zc(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
-        } else {
-          mma_e4m3(d, make_uint4(r0.x, r1.x, r0.y, r1.y), xr[j].x, xr[j].y);
-        }
-        mma_e4m3(d, make_uint4(r0.z, r1.z, r0.w, r1.w), xr[j].z, xr[j].w);
-      }
-      a0 = fmaf(f[kb], d[0] + d[1] * 0.03125f, a0);
-      a1 = fmaf(f[kb], d[2] + d[3] * 0.03125f, a1);
-    }
-    if (rg == 0) {
-      acc[0] = a0;
-      acc[1] = a1;
-    } else {
-      acc[2] = a0;
-      acc[3] = a1;
-    }
+  for (int kb = 0; kb < 4; ++kb) {
+    a0 = fmaf(f[kb], d[kb][0] + d[kb][1] * 0.03125f, a0);
+    a1 = fmaf(f[kb], d[kb][2] + d[kb][3] * 0.03125f, a1);
   }
 }
 
@@ -562,7 +590,6 @@ struct StCtx {
   float* red;
   unsigned long long* misc;
   int* flag;
-  float* attn;         // ST_ATTN_SMEM bytes of attention scratch
   uint32_t full0, empty0;
   unsigned* abort_flag;
   unsigned* timeline;  // optional (see StProgram)
@@ -583,12 +610,13 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
   const int per = S.C / nslice;
   unsigned long long am_best = 0;
   bool good = true;
-  uint64_t blocked = 0;  // timeline only: warp 0's wait for copies to land
+  uint64_t blocked = 0, comp = 0;  // timeline only: warp 0's wait for copies to land, its chunk math
   for (int ub = u0; ub < u1; ub += upb) {
     const int ue = min(u1, ub + upb);
     const int nit = (ue - ub) * ipu;
     const uint32_t m0 = n + (uint32_t)(ub - u0) * ipu;
-    for (int q = warp; q < nit && good; q += ST_CW) {
+    const int pair_id = warp >> 1, rg = warp & 1;
+    for (int q = pair_id; q < nit && good; q += ST_PAIRS) {
       const uint32_t m = m0 + q, slot = m % ST_SLOTS;
       if (!(X.timeline ? mbar_test_wait(X.full0 + 8 * slot, (m / ST_SLOTS) & 1u)
                        : mbar_try_wait(X.full0 + 8 * slot, (m / ST_SLOTS) & 1u))) {
@@ -602,19 +630,20 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
       const int u = ub + q / ipu, i = q % ipu;
       const int t = u / nslice, sl = u - t * nslice;
       const int c = sl * per + (pair ? (i >> 1) : i);
-      float acc[4];
-      st_chunk(X.ring + slot * ST_CHUNK, X.xh, X.xl, X.xinv, c, lane, acc);
+      float a0, a1;
+      const long long tc = X.timeline ? clock64() : 0;
+      st_chunk(X.ring + slot * ST_CHUNK, X.xh, X.xl, X.xinv, c, rg, lane, a0, a1);
+      if (X.timeline) comp += (uint64_t)(clock64() - tc);
       __syncwarp();
-      if (lane == 0) mbar_arrive(X.empty0 + 8 * slot);
+      if (lane == 0) mbar_arrive(X.empty0 + 8 * slot);  // one of the pair's two arrivals
       if ((lane & 3) == 0) {
-        float* pq = X.part + q * ST_ROWS + (lane >> 2);
-        pq[0] = acc[0];
-        pq[8] = acc[1];
-        pq[16] = acc[2];
-        pq[24] = acc[3];
+        float* pq = X.part + q * ST_ROWS + 16 * rg + (lane >> 2);
+        pq[0] = a0;
+        pq[8] = a1;
       }
     }
     named_bar(1, ST_NT);
+    if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_CHUNKS, (unsigned)globaltimer_ns());
     for (int idx = tid; idx < (ue - ub) * ST_ROWS && good; idx += ST_NT) {
       const int ul = idx / ST_ROWS, r = idx % ST_ROWS;
       const int u = ub + ul;
@@ -642,7 +671,10 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
     named_bar(1, ST_NT);
   }
   n += (uint32_t)(u1 - u0) * ipu;
-  if (tid == 0) st_tl_put(X.timeline, X.stage, ST_TL_CBLOCK, (unsigned)blocked);
+  if (tid == 0) {
+    st_tl_put(X.timeline, X.stage, ST_TL_CBLOCK, (unsigned)blocked);
+    st_tl_put(X.timeline, X.stage, ST_TL_WCOMP, (unsigned)comp);
+  }
   if (S.am_ws) st_argmax_finish(S, am_best, X.misc);
 }
 
@@ -759,25 +791,45 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
     }
     named_bar(1, ST_NT);
     if (tid == 0)
-      for (int i = 0; i < ST_GDN_SLOTS; ++i) mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
+      for (int i = 0; i < ST_GDN_SLOTS; ++i) {  // a slot's empty barrier takes two arrivals
+        mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
+        mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
+      }
     n += ST_GDN_SLOTS;
   }
 }
 
-// Attention units on the consumer warps, in a scratch region of their own
-// (the KV rows are read directly, not streamed through the ring).  The step
+// Attention units on the consumer warps, each over ST_ATTN_SLOTS contiguous
+// ring slots of scratch (the producer hands them over in sequence, aligned so
+// they never wrap the ring; the KV rows are read directly).  The step
 // kernel carries the Qwen3.5 layout only (head dim 256, four query heads per
 // KV head): two positions per warp in flight and the queries read from
 // shared memory keep the unit inside this kernel's register budget (9 warps:
 // 168 registers a thread); other layouts use the per-launch attention kernel.
-__device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X) {
+__device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32_t& n) {
+  const int tid = threadIdx.x;
   int u0, u1;
   st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
   for (int u = u0; u < u1; ++u) {
-    const int kh = u / S.attn.nsplit, split = u - kh * S.attn.nsplit;
-    int* s_last = X.flag + 1;
-    attn_unit<256, 4, 2, false>(S.attn, kh, split, X.attn, s_last);
+    const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
+    bool ok = true;
+    if (tid == 0)
+      for (int i = 0; i < cnt && ok; ++i) {
+        const uint32_t m = n + i;
+        ok = st_mbar_wait(X.full0 + 8 * (m % ST_SLOTS), (m / ST_SLOTS) & 1u, X.abort_flag);
+      }
+    if (named_bar_and(1, ST_NT, ok)) {
+      float* scratch = reinterpret_cast<float*>(X.ring + ((n + cnt - ST_ATTN_SLOTS) % ST_SLOTS) * ST_CHUNK);
+      const int kh = u / S.attn.nsplit, split = u - kh * S.attn.nsplit;
+      attn_unit<256, 4, 2, false>(S.attn, kh, split, scratch, X.flag + 1);
+    }
     named_bar(1, ST_NT);
+    if (tid == 0)
+      for (int i = 0; i < cnt; ++i) {  // a slot's empty barrier takes two arrivals
+        mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
+        mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
+      }
+    n += cnt;
   }
 }
 
@@ -793,7 +845,6 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   X.red = reinterpret_cast<float*>(st_smem + StSmem::red);
   X.misc = reinterpret_cast<unsigned long long*>(st_smem + StSmem::misc);
   X.flag = reinterpret_cast<int*>(X.misc + 16);
-  X.attn = reinterpret_cast<float*>(st_smem + StSmem::attn);
   X.full0 = sbase + StSmem::bars;
   X.empty0 = X.full0 + 8 * ST_SLOTS;
   X.abort_flag = P.abort_flag;
@@ -802,7 +853,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST_SLOTS; ++i) {
       mbar_init(X.full0 + 8 * i, 1);
-      mbar_init(X.empty0 + 8 * i, 1);
+      mbar_init(X.empty0 + 8 * i, 2);  // released by both warps of a pair
     }
     mbar_fence_init();
   }
@@ -831,7 +882,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     } else if (kind == ST_GDN) {
       st_gdn(S, X, n);
     } else {
-      st_attn(S, X);
+      st_attn(S, X, n);
     }
     named_bar(1, ST_NT);
     if (tid == 0) {

@@ -198,7 +198,7 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     const int G = in.a_heads / in.a_kv;
     const int smem = 4 * (G * in.a_dim + ATTN_WARPS * G * in.a_dim + 2 * ATTN_WARPS * G + 2 * in.a_dim +
                           ATTN_WARPS * in.a_dim);
-    if (in.a_dim != 256 || G != 4 || smem > ST_ATTN_SMEM) return cudaErrorNotSupported;
+    if (in.a_dim != 256 || G != 4 || smem > ST_ATTN_SLOTS * ST_CHUNK) return cudaErrorNotSupported;
     AttnArgs& a = o.attn;
     a = AttnArgs{};
     a.q = static_cast<const bf16*>(in.a_q);

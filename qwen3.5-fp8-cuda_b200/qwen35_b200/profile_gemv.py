@@ -52,10 +52,17 @@ def gemv_bytes(n: int, k: int) -> int:
     return n * k + ((n + 127) // 128) * (k // 128) * 2 + 2 * k + 2 * n
 
 
-def time_shapes(peak_gbs: float, shapes=DECODE_SHAPES, launches: int = 64, replays: int = 10) -> list:
-    """Mean time per launch of each shape (see the module docstring)."""
+def time_shapes(peak_gbs: float, shapes=DECODE_SHAPES, launches: int = 64, replays: int = 10, ref_lib=None,
+                chained: bool = True) -> list:
+    """Mean time per launch of each shape (see the module docstring).
+
+    ``ref_lib``: another library exporting ``launch_gemv_v4_extern`` with the
+    reference's signature (e.g. the reference's own kernels built for
+    sm_100a); when given, its entry point is timed instead of ours, as
+    ``abi``.  ``chained=False`` skips the PDL-chained leg."""
     P = ctypes.c_void_p
     lib = _lib.fused()
+    abi_lib = ref_lib if ref_lib is not None else lib
     out = []
     for role, n, k in shapes:
         wb = n * k
@@ -68,20 +75,22 @@ def time_shapes(peak_gbs: float, shapes=DECODE_SHAPES, launches: int = 64, repla
         yf = torch.empty(n, dtype=torch.float32, device="cuda")
 
         def abi(i, st):
-            lib.launch_gemv_v4_extern(P(x.data_ptr()), P(ws[i].data_ptr()), P(s.data_ptr()), P(y.data_ptr()),
+            abi_lib.launch_gemv_v4_extern(P(x.data_ptr()), P(ws[i].data_ptr()), P(s.data_ptr()), P(y.data_ptr()),
                                       n, k, k // 128, st)
 
-        def chained(i, st):
+        def chained_leg(i, st):
             _lib.check(lib.qwen_linear_partial(P(x.data_ptr()), P(ws[i].data_ptr()), P(s.data_ptr()), n, k,
                                                k // 128, P(yf.data_ptr()), st), "qwen_linear_partial")
 
         row = {"role": role, "shape": f"{n}x{k}", "bytes": gemv_bytes(n, k), "copies": copies,
                "cycled_mb": round(copies * wb / 2**20, 1), "l2_resident": copies * wb <= L2_BYTES}
-        for name, fn in (("abi", abi), ("chained", chained)):
+        legs = [("abi", abi)] + ([("chained", chained_leg)] if chained else [])
+        for name, fn in legs:
             st = P(torch.cuda.current_stream().cuda_stream)
             for i in range(copies):  # tensor maps built outside the capture
                 fn(i, st)
-            _lib.check_last(f"gemv {n}x{k}")
+            if ref_lib is None:
+                _lib.check_last(f"gemv {n}x{k}")
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):

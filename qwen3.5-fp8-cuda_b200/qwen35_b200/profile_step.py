@@ -20,7 +20,10 @@ name, where the step's time goes:
   issuing the stage / consumer warp 0 was blocked on copies not yet landed
   (a producer blocked means the consumers set the pace; consumers blocked
   means the stream does);
-* ``pro``: median time from the stage's start to its x prologue being done.
+* ``pro``: median time from the stage's start to its x prologue being done;
+* ``chunk``: median time from the prologue's end to the last batch's chunk
+  math being done; ``wcomp``: consumer warp 0's SM clock cycles (thousands)
+  inside the chunk math.
 
 Also prints the step time measured with CUDA events over ``--steps`` steps.
 """
@@ -34,7 +37,7 @@ import statistics
 import torch
 
 KINDS = {0: "gemv", 1: "gdn", 2: "attn"}
-NF = 8  # timeline words per (stage, CTA)
+NF = 10  # timeline words per (stage, CTA)
 
 
 def stage_names(cfg):
@@ -48,7 +51,7 @@ def stage_names(cfg):
 
 
 def timeline(eng):
-    """One step with the timeline on: [stages, grid, 8] int64 (stamps in ns from the earliest one)."""
+    """One step with the timeline on: [stages, grid, 10] int64 (stamps in ns from the earliest one)."""
     ns, grid = len(eng.stages), eng.grid
     buf = torch.zeros(ns * grid * NF, dtype=torch.int32, device=eng.device)
     eng.lib.qwen_step_set_timeline(eng.prog, ctypes.c_void_p(buf.data_ptr()))
@@ -58,7 +61,9 @@ def timeline(eng):
     t = (buf.cpu().to(torch.int64) & 0xFFFFFFFF).view(ns, grid, NF)
     base = int(t[0, :, 0].min())
     t[:, :, :5] = (t[:, :, :5] - base) % (1 << 32)
-    t[:, :, 7] = (t[:, :, 7] - base) % (1 << 32)
+    for f in (7, 8):
+        nz = t[:, :, f] != 0
+        t[:, :, f] = torch.where(nz, (t[:, :, f] - base) % (1 << 32), torch.zeros_like(t[:, :, f]))
     return t
 
 
@@ -74,7 +79,9 @@ def summarize(cfg, t):
                          sync=int(start.median()) - prev_end, work_med=statistics.median(work), work_max=max(work),
                          lead=int(start.median()) - int(p1.median()),
                          pblk=int(t[s, :, 5].median()), cblk=int(t[s, :, 6].median()),
-                         pro=max(0, int((t[s, :, 7] - start).median())) if int(t[s, :, 7].max()) else 0))
+                         pro=max(0, int((t[s, :, 7] - start).median())) if int(t[s, :, 7].max()) else 0,
+                         chunks=max(0, int((t[s, :, 8] - t[s, :, 7]).median())) if int(t[s, :, 8].max()) else 0,
+                         wcomp=int(t[s, :, 9].median())))
         prev_end = last_end
     return rows
 
@@ -85,17 +92,20 @@ def report(cfg, t, per_stage=False, out=print):
     out(f"timeline step: {total / 1000:.1f} us")
     agg = {}
     for r in rows:
-        a = agg.setdefault(r["name"], dict(n=0, span=0, sync=0, work_med=0, work_max=0, lead=0, pblk=0, cblk=0, pro=0))
+        a = agg.setdefault(r["name"], dict(n=0, span=0, sync=0, work_med=0, work_max=0, lead=0, pblk=0, cblk=0, pro=0, chunks=0,
+                                             wcomp=0))
         a["n"] += 1
-        for k in ("span", "sync", "work_med", "work_max", "lead", "pblk", "cblk", "pro"):
+        for k in ("span", "sync", "work_med", "work_max", "lead", "pblk", "cblk", "pro", "chunks", "wcomp"):
             a[k] += r[k]
     out(f"{'stage':10s} {'n':>4s} {'span us':>9s} {'share':>6s} {'sync us':>8s} {'work med':>9s} {'work max':>9s} "
-        f"{'lead us':>8s} {'pblk us':>8s} {'cblk us':>8s} {'pro us':>7s}  (per-stage means)")
+        f"{'lead us':>8s} {'pblk us':>8s} {'cblk us':>8s} {'pro us':>7s} {'chunk us':>8s} {'wcomp kcyc':>10s}"
+        "  (per-stage means)")
     for name, a in agg.items():
         n = a["n"]
         out(f"{name:10s} {n:4d} {a['span'] / n / 1000:9.2f} {a['span'] / total:6.1%} {a['sync'] / n / 1000:8.2f} "
             f"{a['work_med'] / n / 1000:9.2f} {a['work_max'] / n / 1000:9.2f} {a['lead'] / n / 1000:8.2f} "
-            f"{a['pblk'] / n / 1000:8.2f} {a['cblk'] / n / 1000:8.2f} {a['pro'] / n / 1000:7.2f}")
+            f"{a['pblk'] / n / 1000:8.2f} {a['cblk'] / n / 1000:8.2f} {a['pro'] / n / 1000:7.2f} "
+            f"{a['chunks'] / n / 1000:8.2f} {a['wcomp'] / n / 1000:10.2f}")
     if per_stage:
         for r in rows:
             out(str(r))
