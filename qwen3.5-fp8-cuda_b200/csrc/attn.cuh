@@ -59,8 +59,17 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
                                                const float* sn, int rot, float eps, float* vals_sm, float (&v)[D / 32],
                                                int lane) {
   constexpr int EPL = D / 32;
+  // every load first (the head, the norm weights, this lane's RoPE factors):
+  // one round trip instead of one per phase
+  float nw[EPL], cf[EPL], sf[EPL];
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) v[e] = bf2f(__ldcg(src + lane * EPL + e));
+  for (int e = 0; e < EPL; ++e) {
+    const int i = lane * EPL + e;
+    v[e] = bf2f(__ldcg(src + i));
+    nw[e] = norm_w ? norm_w[i] : 0.f;
+    cf[e] = cs && i < rot ? cs[i] : 0.f;
+    sf[e] = sn && i < rot ? sn[i] : 0.f;
+  }
   if (norm_w) {
     float ss = 0.f;
 #pragma unroll
@@ -68,7 +77,7 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / (float)D + eps);
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) v[e] = bfround(v[e] * r * (1.0f + norm_w[lane * EPL + e]));
+    for (int e = 0; e < EPL; ++e) v[e] = bfround(v[e] * r * (1.0f + nw[e]));
   }
   if (cs) {
 #pragma unroll
@@ -79,9 +88,9 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
     for (int e = 0; e < EPL; ++e) {
       const int i = lane * EPL + e;
       if (i < half) {
-        v[e] = bfround(vals_sm[i] * cs[i] - vals_sm[i + half] * sn[i]);
+        v[e] = bfround(vals_sm[i] * cf[e] - vals_sm[i + half] * sf[e]);
       } else if (i < rot) {
-        v[e] = bfround(vals_sm[i] * cs[i] + vals_sm[i - half] * sn[i]);
+        v[e] = bfround(vals_sm[i] * cf[e] + vals_sm[i - half] * sf[e]);
       }
     }
     __syncwarp();
@@ -91,11 +100,16 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
 // One (KV head, split) unit of the attention step on ATTN_WARPS warps (threads
 // 0 .. ATTN_WARPS*32-1 of the caller, named barrier 1).  `asmem` holds
 // attn_smem_bytes<D, G>() bytes; `s_last` is one shared int.  Every exit is
-// uniform over the calling threads.  U: positions per warp in flight; QREG:
+// uniform over the calling threads.  `tl` (optional, profiling): thread 0
+// stores %globaltimer stamps after the query / key / value preparation, after
+// the split's partials are published, and (last unit only) after the combine
+// into tl[0], tl[1], tl[2].  `pos_known` >= 0: the position, already read by
+// the caller (else *a.pos_ptr).  U: positions per warp in flight; QREG:
 // the scaled queries held in registers (else re-read from shared memory per
 // position, for callers with a tighter register budget).
 template <int D, int G, int U = 4, bool QREG = true>
-__device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, float* asmem, int* s_last_p) {
+__device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, float* asmem, int* s_last_p,
+                                          unsigned* tl = nullptr, int pos_known = -1) {
   constexpr int EPL = D / 32;
   constexpr int NT = ATTN_WARPS * 32;
   float* qsm = asmem;                       // [G][D] scaled query
@@ -107,7 +121,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
   int& s_last = *s_last_p;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int pos = a.pos_ptr ? __ldcg(a.pos_ptr) : a.pos_const;
+  const int pos = pos_known >= 0 ? pos_known : (a.pos_ptr ? __ldcg(a.pos_ptr) : a.pos_const);
   if (pos < 0 || pos >= a.max_seq) {  // uniform over the grid: every unit leaves
     if (threadIdx.x == 0 && kh == 0 && split == 0) qwen_err_set(ERR_POS_RANGE);
     return;
@@ -150,6 +164,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
     }
   }
   named_bar(1, NT);
+  if (tl && threadIdx.x == 0) tl[0] = (unsigned)globaltimer_ns();
 
   // ---- Phase B: positions of this split ----
   float qr[QREG ? G : 1][EPL];
@@ -284,70 +299,123 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
     s_last = prev == (unsigned)(nsplit - 1);
   }
   named_bar(1, NT);
+  if (tl && threadIdx.x == 0) tl[1] = (unsigned)globaltimer_ns();
   if (!s_last) return;
   __threadfence();
   const int n_active = (total + chunk - 1) / chunk;
-  // Split weights: warp g handles head g with its lanes over the splits
-  // (the per-warp output area holds f_s = exp(m_s - M)); then every thread
-  // adds its (head, channel) over the splits with 8 split rows in flight.
+  // Split weights f_s = exp(m_s - M) (held in the per-warp output area),
+  // then every thread adds its (head, channel) pairs over the splits.
   float* fac = wo;
   constexpr int FCAP = ATTN_WARPS * D;  // splits per head that fit
   const bool fits = n_active <= FCAP;
   if (fits) {
+    // split weights: warp g, lanes over the splits; (M, L) of a split is one
+    // 8-byte load, every lane's loads issued before the reductions
+    constexpr int MAXL = 4;  // splits per lane held in registers (n_active <= 128)
     for (int g = warp; g < G; g += ATTN_WARPS) {
       const float* base = a.ws_part + (size_t)(kh * G + g) * nsplit * (D + 2);
-      float M = -INFINITY;
-      for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(base + s * (D + 2)));
-      M = warp_max(M);
-      float L = 0.f;
-      for (int s = lane; s < n_active; s += 32) {
-        const float ms = __ldcg(base + s * (D + 2));
-        const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-        L += __ldcg(base + s * (D + 2) + 1) * f;
-        fac[g * FCAP + s] = f;
+      float M = -INFINITY, L = 0.f;
+      if (n_active <= 32 * MAXL) {
+        float2 ml[MAXL];
+#pragma unroll
+        for (int k = 0; k < MAXL; ++k) {
+          const int sp = lane + 32 * k;
+          ml[k] = sp < n_active ? __ldcg(reinterpret_cast<const float2*>(base + sp * (D + 2)))
+                                : make_float2(-INFINITY, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < MAXL; ++k) M = fmaxf(M, ml[k].x);
+        M = warp_max(M);
+#pragma unroll
+        for (int k = 0; k < MAXL; ++k) {
+          const int sp = lane + 32 * k;
+          const float f = ml[k].x == -INFINITY ? 0.f : expf(ml[k].x - M);
+          L += ml[k].y * f;
+          if (sp < n_active) fac[g * FCAP + sp] = f;
+        }
+      } else {
+        for (int sp = lane; sp < n_active; sp += 32) M = fmaxf(M, __ldcg(base + sp * (D + 2)));
+        M = warp_max(M);
+        for (int sp = lane; sp < n_active; sp += 32) {
+          const float ms = __ldcg(base + sp * (D + 2));
+          const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+          L += __ldcg(base + sp * (D + 2) + 1) * f;
+          fac[g * FCAP + sp] = f;
+        }
       }
       L = warp_sum(L);
       if (lane == 0) wl[g] = L;
     }
-  }
-  named_bar(1, NT);
-  for (int idx = threadIdx.x; idx < G * D; idx += NT) {
-    const int g = idx / D, d = idx % D;
-    const int h = kh * G + g;
-    const float* base = a.ws_part + (size_t)h * nsplit * (D + 2);
-    float Os = 0.f, Ls;
-    if (fits) {
-      const float* fg = fac + g * FCAP;
-      int s = 0;
-      for (; s + 8 <= n_active; s += 8) {
-        float o[8];
+    named_bar(1, NT);
+    // every thread adds its PER (head, channel) pairs over the splits in
+    // split order, four splits' loads of all its pairs in flight at a time
+    constexpr int PER = (G * D + NT - 1) / NT;
+    float Os[PER], gv[PER];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = __ldcg(base + (s + j) * (D + 2) + 2 + d);
+    for (int k = 0; k < PER; ++k) {
+      const int idx = threadIdx.x + k * NT;
+      Os[k] = 0.f;
+      gv[k] = 0.f;
+      if (idx < G * D && a.gate)
+        gv[k] = bf2f(__ldcg(a.gate + (size_t)(kh * G + idx / D) * a.q_stride + idx % D));
+    }
+    constexpr int SPI = PER <= 4 ? 8 : 4;  // splits per iteration: up to 32 loads in flight
+    for (int s = 0; s < n_active; s += SPI) {
+      float o[SPI][PER];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) Os = fmaf(o[j], fg[s + j], Os);
-      }
-      for (; s < n_active; ++s) Os = fmaf(__ldcg(base + s * (D + 2) + 2 + d), fg[s], Os);
-      Ls = wl[g];
-    } else {
+      for (int j = 0; j < SPI; ++j)
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+          const int idx = threadIdx.x + k * NT;
+          o[j][k] = (idx < G * D && s + j < n_active)
+                        ? __ldcg(a.ws_part + ((size_t)(kh * G + idx / D) * nsplit + s + j) * (D + 2) + 2 + idx % D)
+                        : 0.f;
+        }
+#pragma unroll
+      for (int j = 0; j < SPI; ++j)
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+          const int idx = threadIdx.x + k * NT;
+          if (idx < G * D && s + j < n_active) Os[k] = fmaf(o[j][k], fac[(idx / D) * FCAP + s + j], Os[k]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int idx = threadIdx.x + k * NT;
+      if (idx >= G * D) continue;
+      const int g = idx / D, d = idx % D;
+      bf16 ob = f2bf(Os[k] * (1.0f / wl[g]));
+      if (a.gate) ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv[k]))));
+      a.out[(size_t)(kh * G + g) * D + d] = ob;
+    }
+  } else {
+    named_bar(1, NT);
+    for (int idx = threadIdx.x; idx < G * D; idx += NT) {
+      const int g = idx / D, d = idx % D;
+      const int h = kh * G + g;
+      const float* base = a.ws_part + (size_t)h * nsplit * (D + 2);
+      float Os = 0.f, Ls = 0.f;
       float M = -INFINITY;
-      for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(base + s * (D + 2)));
-      Ls = 0.f;
-      for (int s = 0; s < n_active; ++s) {
-        const float ms = __ldcg(base + s * (D + 2));
+      for (int sp = 0; sp < n_active; ++sp) M = fmaxf(M, __ldcg(base + sp * (D + 2)));
+      for (int sp = 0; sp < n_active; ++sp) {
+        const float ms = __ldcg(base + sp * (D + 2));
         if (ms == -INFINITY) continue;
         const float f = expf(ms - M);
-        Ls += __ldcg(base + s * (D + 2) + 1) * f;
-        Os += __ldcg(base + s * (D + 2) + 2 + d) * f;
+        Ls += __ldcg(base + sp * (D + 2) + 1) * f;
+        Os += __ldcg(base + sp * (D + 2) + 2 + d) * f;
       }
+      bf16 ob = f2bf(Os * (1.0f / Ls));
+      if (a.gate) {
+        const float gv = bf2f(__ldcg(a.gate + (size_t)h * a.q_stride + d));
+        ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv))));
+      }
+      a.out[(size_t)h * D + d] = ob;
     }
-    bf16 ob = f2bf(Os * (1.0f / Ls));
-    if (a.gate) {
-      const float gv = bf2f(__ldcg(a.gate + (size_t)h * a.q_stride + d));
-      ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv))));
-    }
-    a.out[(size_t)h * D + d] = ob;
   }
-  if (threadIdx.x == 0) a.ws_count[kh] = 0u;
+  if (threadIdx.x == 0) {
+    a.ws_count[kh] = 0u;
+    if (tl) tl[2] = (unsigned)globaltimer_ns();
+  }
 }
 
 template <int D, int G>

@@ -44,6 +44,13 @@
 
 namespace qwen {
 
+#ifndef QWEN_STEP_SLOTS
+#define QWEN_STEP_SLOTS 12
+#endif
+#ifndef QWEN_STEP_ATTN_SLOTS
+#define QWEN_STEP_ATTN_SLOTS 3
+#endif
+
 enum : int { ST_GEMV = 0, ST_GDN = 1, ST_ATTN = 2 };
 // x prologue of a GEMV stage
 enum : int {
@@ -69,7 +76,7 @@ constexpr int ST_CHUNK = ST_WBYTES + 16;       // + four FP32 block scales
 // the warp pairs: items m and m + ST_SLOTS share a slot and go to the same
 // pair, so no thread ever waits on a phase beyond the next one of a slot's
 // barrier (a parity wait cannot tell those apart).
-constexpr int ST_SLOTS = 12;
+constexpr int ST_SLOTS = QWEN_STEP_SLOTS;
 constexpr int ST_CW = 8;                       // consumer warps
 constexpr int ST_PAIRS = ST_CW / 2;            // consumer warp pairs (one chunk each)
 constexpr int ST_NT = ST_CW * 32;
@@ -78,33 +85,23 @@ constexpr int ST_MAXK = 9216;                  // longest GEMV input
 constexpr int ST_MAXB = (ST_MAXK / 128 + ST_CW - 1) / ST_CW;  // 128-blocks per warp in the prologue
 constexpr int ST_NORM_MAXK = 3072;             // longest input of a normalising (or embedding) prologue
 constexpr int ST_NORM_MAXB = ST_NORM_MAXK / 128 / ST_CW;
+constexpr int ST_SL_REG = 4;                   // K-slice rows a prologue loads in one round trip
 constexpr int ST_BATCH = 48;                   // chunk partials held before a reduction
 constexpr int ST_MAX_SEG = 4;
-constexpr int ST_ATTN_SLOTS = 3;               // contiguous ring slots of scratch for an attention unit
+constexpr int ST_ATTN_SLOTS = QWEN_STEP_ATTN_SLOTS;  // contiguous ring slots of scratch for an attention unit
 constexpr int ST_GDN_D = 128;                  // GatedDeltaNet head dim of the step kernel
 constexpr int ST_GDN_SLOTS = ST_GDN_D * ST_GDN_D * 4 / ST_WBYTES;  // 4: one head's FP32 state
 constexpr int ST_GDN_KPS = ST_WBYTES / (ST_GDN_D * 4);            // 32 key rows of state per slot
 static_assert(ST_SLOTS % ST_PAIRS == 0, "items m and m + ST_SLOTS must go to the same consumer warp pair");
 static_assert(ST_SLOTS % ST_ATTN_SLOTS == 0, "attention scratch groups must not wrap the ring");
+// an attention unit waits for its alignment padding plus its scratch slots at
+// once (up to 2 * ST_ATTN_SLOTS - 1 items): they must fit the ring together
+static_assert(2 * ST_ATTN_SLOTS - 1 <= ST_SLOTS, "attention padding + scratch must fit the ring");
 static_assert(ST_GDN_SLOTS <= ST_SLOTS, "a head's state must fit the ring");
 static_assert(ST_NT == ATTN_WARPS * 32, "attention units run on the consumer warps");
 
-// Shared memory plan (bytes from the dynamic shared memory base).
-struct StSmem {
-  static constexpr int ring = 0;
-  static constexpr int xh = ST_SLOTS * ST_CHUNK;
-  static constexpr int xl = xh + ST_MAXK;
-  static constexpr int xinv = xl + ST_MAXK;
-  static constexpr int part = xinv + ST_MAXK / 128 * 4;
-  static constexpr int red = part + ST_BATCH * ST_ROWS * 4;
-  static constexpr int misc = red + 64 * 4;
-  static constexpr int bars = misc + 32 * 8;
-  static constexpr int total = bars + 2 * ST_SLOTS * 8;
-};
-static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8 == 0, "alignment");
-static_assert(StSmem::total <= 227 * 1024, "shared memory");
 
-struct StStage {
+struct alignas(16) StStage {
   int kind;
   // GEMV
   int K, C;            // input length; 512-wide chunks per tile row
@@ -135,12 +132,31 @@ struct StStage {
   int attn_dim, attn_g;
 };
 
+// Shared memory plan (bytes from the dynamic shared memory base).
+struct StSmem {
+  static constexpr int ring = 0;
+  static constexpr int xh = ST_SLOTS * ST_CHUNK;
+  static constexpr int xl = xh + ST_MAXK;
+  static constexpr int xinv = xl + ST_MAXK;
+  static constexpr int part = xinv + ST_MAXK / 128 * 4;
+  static constexpr int red = part + ST_BATCH * ST_ROWS * 4;
+  static constexpr int misc = red + 64 * 4;
+  static constexpr int bars = misc + 32 * 8;
+  // the descriptors of the running stage and the next one (16-byte copies)
+  static constexpr int desc = (bars + 2 * ST_SLOTS * 8 + 15) / 16 * 16;
+  static constexpr int total = desc + 2 * (int)sizeof(StStage);
+};
+static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8 == 0, "alignment");
+static_assert(sizeof(StStage) % 16 == 0, "stage descriptors are copied in 16-byte pieces");
+static_assert(StSmem::total <= 227 * 1024, "shared memory");
+
 struct StProgram {
   const StStage* stages;
   int nstages;
   unsigned* counters;    // [nstages + 1]: CTAs done with each stage, then with the step
   unsigned* abort_flag;  // set by a timed-out wait; every wait then gives up at once
   unsigned* timeline;    // optional [nstages][grid][ST_TL]: %globaltimer (low 32 bits, ns) per stage and CTA
+  const int* pos;        // decode position read by the attention stages (constant within a step), or null
 };
 
 // Timeline fields of one (stage, CTA): the consumers' wait for the previous
@@ -149,7 +165,11 @@ struct StProgram {
 // Also, in ns: the producer's time blocked on a full ring while issuing the
 // stage, and consumer warp 0's time blocked on copies not yet landed.
 // Then, for GEMV stages: the stamps at which the x prologue was done and the
-// last batch's chunks were, and consumer warp 0's SM cycles inside the chunk math.
+// last batch's chunks were, and consumer warp 0's SM cycles inside the chunk
+// math; for GatedDeltaNet stages the stamps at which the last head's inputs
+// had arrived and its state update was done; for attention stages the
+// stamps after the unit's q / k / v preparation, after its partials were
+// published and (the combining unit) after the combine.
 enum : int {
   ST_TL_WAIT = 0, ST_TL_START = 1, ST_TL_END = 2, ST_TL_P0 = 3, ST_TL_P1 = 4, ST_TL_PBLOCK = 5, ST_TL_CBLOCK = 6,
   ST_TL_PRO = 7, ST_TL_CHUNKS = 8, ST_TL_WCOMP = 9, ST_TL = 10
@@ -351,8 +371,9 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
 // Every load of a phase is issued before any is used: while the weight
 // stream saturates HBM an L2 round trip takes ~0.5 us, so dependent loads
 // would cost a round trip each.  MB: 128-blocks per warp this instantiation
-// holds (norm stages: K <= 3072).
-template <int MB>
+// holds (norm stages: K <= 3072); SLR: K-slice rows loaded with the first
+// round trip (0 for the plain prologue).
+template <int MB, int SLR>
 __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8_t* xl, float* xinv, float* red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = S.K, nb = K >> 7, pro = S.pro, nsl = S.sl_in_count, sl_stride = S.sl_stride;
@@ -370,9 +391,12 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   }
   const bf16* src = pro == STP_SLICES_NORM ? S.res : xin;
   bf16* h_out = (blockIdx.x == 0 && (pro == STP_SLICES_NORM || pro == STP_EMBED_NORM)) ? S.h_out : nullptr;
-  // phase 1: input (or residual) and norm weights, all in flight
+  // every load at once (the input or residual, the norm weights and up to
+  // ST_SL_REG K-slice rows), added in slice order once they have arrived
   uint2 raw[MB];
   float4 wv[MB];
+  float4 sp[MB][SLR > 0 ? SLR : 1];
+  const int nreg = pro == STP_SLICES_NORM ? (nsl < SLR ? nsl : SLR) : 0;
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
     const int b = warp + i * ST_CW;
@@ -381,6 +405,9 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
       raw[i] = pro == STP_EMBED_NORM ? __ldg(reinterpret_cast<const uint2*>(src + k0))
                                      : __ldcg(reinterpret_cast<const uint2*>(src + k0));
       if (norm) wv[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k0));
+#pragma unroll
+      for (int c = 0; c < SLR; ++c)
+        if (c < nreg) sp[i][c] = __ldcg(reinterpret_cast<const float4*>(sl_in + (size_t)c * sl_stride + k0));
     }
   }
   float v[MB][4];
@@ -389,33 +416,26 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
     const float2 a01 = bf2x_to_f2(raw[i].x), a23 = bf2x_to_f2(raw[i].y);
     v[i][0] = a01.x; v[i][1] = a01.y; v[i][2] = a23.x; v[i][3] = a23.y;
   }
-  // phase 2: the K-slice partial rows, two slices' loads in flight at a
-  // time, added in slice order
   if (pro == STP_SLICES_NORM) {
     float sum[MB][4];
 #pragma unroll
-    for (int i = 0; i < MB; ++i) sum[i][0] = sum[i][1] = sum[i][2] = sum[i][3] = 0.f;
-    for (int c = 0; c < nsl; c += 2) {
-      const bool two = c + 1 < nsl;
-      float4 p0[MB], p1[MB];
+    for (int i = 0; i < MB; ++i) {
+      sum[i][0] = sum[i][1] = sum[i][2] = sum[i][3] = 0.f;
+#pragma unroll
+      for (int c = 0; c < SLR; ++c)
+        if (c < nreg) {
+          sum[i][0] += sp[i][c].x; sum[i][1] += sp[i][c].y; sum[i][2] += sp[i][c].z; sum[i][3] += sp[i][c].w;
+        }
+    }
+    // slices beyond SLR (rare): one more round trip each, in order
+    for (int c = nreg; c < nsl; ++c)
 #pragma unroll
       for (int i = 0; i < MB; ++i) {
         const int b = warp + i * ST_CW;
-        const float* pp = sl_in + (size_t)c * sl_stride + b * 128 + lane * 4;
-        if (b < nb) {
-          p0[i] = __ldcg(reinterpret_cast<const float4*>(pp));
-          if (two) p1[i] = __ldcg(reinterpret_cast<const float4*>(pp + sl_stride));
-        }
+        if (b >= nb) continue;
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(sl_in + (size_t)c * sl_stride + b * 128 + lane * 4));
+        sum[i][0] += p.x; sum[i][1] += p.y; sum[i][2] += p.z; sum[i][3] += p.w;
       }
-#pragma unroll
-      for (int i = 0; i < MB; ++i) {
-        if (warp + i * ST_CW >= nb) continue;
-        sum[i][0] += p0[i].x; sum[i][1] += p0[i].y; sum[i][2] += p0[i].z; sum[i][3] += p0[i].w;
-        if (two) {
-          sum[i][0] += p1[i].x; sum[i][1] += p1[i].y; sum[i][2] += p1[i].z; sum[i][3] += p1[i].w;
-        }
-      }
-    }
 #pragma unroll
     for (int i = 0; i < MB; ++i)
 #pragma unroll
@@ -601,9 +621,9 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
   int u0, u1;
   st_range(S.nunits, u0, u1);
   if (S.pro == STP_PLAIN)
-    st_prologue<ST_MAXB>(S, X.xh, X.xl, X.xinv, X.red);
+    st_prologue<ST_MAXB, 0>(S, X.xh, X.xl, X.xinv, X.red);
   else
-    st_prologue<ST_NORM_MAXB>(S, X.xh, X.xl, X.xinv, X.red);
+    st_prologue<ST_NORM_MAXB, ST_SL_REG>(S, X.xh, X.xl, X.xinv, X.red);
   if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_PRO, (unsigned)globaltimer_ns());
   const int ipu = S.ipu, nslice = S.nslice, pair = S.pair;
   const int upb = ST_BATCH / ipu > 0 ? ST_BATCH / ipu : 1;
@@ -741,6 +761,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
         s[i] = *reinterpret_cast<const float*>(X.ring + slot * ST_CHUNK + (k % ST_GDN_KPS) * (D * 4) + d * 4);
       }
       named_bar(1, ST_NT);
+      if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_PRO, (unsigned)globaltimer_ns());
       const float tq = X.red[0] + X.red[1] + X.red[2] + X.red[3];
       const float tk = X.red[4] + X.red[5] + X.red[6] + X.red[7];
       const float q_scale = rsqrtf(tq + 1e-6f) * rsqrtf((float)D);
@@ -771,6 +792,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
       }
       red2[kg * D + d] = o;
       named_bar(1, ST_NT);
+      if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_CHUNKS, (unsigned)globaltimer_ns());
       if (kg == 0) {
         const bf16 core = f2bf(red2[d] + red2[D + d]);
         bf16* out = a.out + (size_t)h * D + d;
@@ -821,7 +843,8 @@ __device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32
     if (named_bar_and(1, ST_NT, ok)) {
       float* scratch = reinterpret_cast<float*>(X.ring + ((n + cnt - ST_ATTN_SLOTS) % ST_SLOTS) * ST_CHUNK);
       const int kh = u / S.attn.nsplit, split = u - kh * S.attn.nsplit;
-      attn_unit<256, 4, 2, false>(S.attn, kh, split, scratch, X.flag + 1);
+      unsigned* tl = X.timeline ? X.timeline + ((size_t)X.stage * gridDim.x + blockIdx.x) * ST_TL + ST_TL_PRO : nullptr;
+      attn_unit<256, 4, 2, false>(S.attn, kh, split, scratch, X.flag + 1, tl, X.flag[2]);
     }
     named_bar(1, ST_NT);
     if (tid == 0)
@@ -831,6 +854,17 @@ __device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32
       }
     n += cnt;
   }
+}
+
+// Copies one stage descriptor into shared memory in 16-byte cp.async pieces
+// spread over the consumer threads (each thread waits for its own pieces with
+// cp.async.wait_group 0; a barrier then publishes them).
+__device__ __forceinline__ void st_desc_fetch(uint32_t dst, const StStage* src, int tid) {
+  constexpr int n16 = (int)(sizeof(StStage) / 16);
+  for (int i = tid; i < n16; i += ST_NT)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst + 16u * i),
+                 "l"(reinterpret_cast<const uint4*>(src) + i) : "memory");
+  cp_async_commit();
 }
 
 __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_constant__ StProgram P) {
@@ -851,6 +885,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   X.timeline = P.timeline;
   X.stage = 0;
   if (threadIdx.x == 0) {
+    // the decode position is constant within a step (the LM head stage
+    // increments it last), so attention stages read it once per launch
+    X.flag[2] = P.pos ? __ldcg(P.pos) : -1;
     for (int i = 0; i < ST_SLOTS; ++i) {
       mbar_init(X.full0 + 8 * i, 1);
       mbar_init(X.empty0 + 8 * i, 2);  // released by both warps of a pair
@@ -865,15 +902,26 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   const int tid = threadIdx.x;
   uint32_t n = 0;
   bool alive = true;
+  // Stage descriptors are read from shared memory: the next stage's one is
+  // copied in while the current stage runs, so a stage's first loads do not
+  // wait for its descriptor to come from L2.
+  const StStage* desc = reinterpret_cast<const StStage*>(st_smem + StSmem::desc);
+  st_desc_fetch(sbase + StSmem::desc, P.stages, tid);
   for (int s = 0; s < P.nstages; ++s) {
-    const StStage& S = P.stages[s];
     if (tid == 0) st_stamp(P, s, ST_TL_WAIT);
+    cp_async_wait<0>();  // this thread's pieces of stage s's descriptor
     if (s > 0) {
       bool ok = true;
       if (tid == 0) ok = st_wait_count(P.counters + s - 1, gridDim.x, P.abort_flag);
       alive = named_bar_and(1, ST_NT, ok);
       if (!alive) break;
+    } else {
+      named_bar(1, ST_NT);
     }
+    const StStage& S = desc[s & 1];
+    // the other buffer held stage s - 1, which every consumer has finished
+    if (s + 1 < P.nstages)
+      st_desc_fetch(sbase + StSmem::desc + ((s + 1) & 1) * (uint32_t)sizeof(StStage), P.stages + s + 1, tid);
     if (tid == 0) st_stamp(P, s, ST_TL_START);
     X.stage = s;
     const int kind = S.kind;

@@ -20,6 +20,7 @@ struct StepProgramHost {
   qwen::StStage* d_stages = nullptr;
   unsigned* d_counters = nullptr;  // nstages + 1 counters, then the abort flag
   unsigned* timeline = nullptr;    // optional per-stage timestamps (qwen_step_set_timeline)
+  const int* pos = nullptr;        // the attention stages' position (all of them share one)
 };
 
 bool g_step_attr_done[64] = {};
@@ -284,8 +285,15 @@ int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_
     conv.push_back(o);
     ins.push_back(stages[i]);
   }
+  const int* pos = nullptr;
+  for (int i = 0; i < nstages; ++i)
+    if (stages[i].kind == QWEN_STEP_ATTN) {
+      if (pos && stages[i].a_pos != pos) return record(cudaErrorInvalidValue);  // one position per program
+      pos = stages[i].a_pos;
+    }
   StepProgramHost* p = new StepProgramHost();
   p->dev = dev;
+  p->pos = pos;
   p->grid = grid;
   p->nstages = nstages;
   e = cudaMalloc(&p->d_stages, sizeof(qwen::StStage) * nstages);
@@ -312,6 +320,7 @@ int qwen_step_launch(void* program, cudaStream_t stream) {
   P.counters = p->d_counters;
   P.abort_flag = p->d_counters + p->nstages + 1;
   P.timeline = p->timeline;
+  P.pos = p->pos;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p->grid);
   cfg.blockDim = dim3(qwen::ST_THREADS);

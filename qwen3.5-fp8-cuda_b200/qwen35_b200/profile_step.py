@@ -23,7 +23,10 @@ name, where the step's time goes:
 * ``pro``: median time from the stage's start to its x prologue being done;
 * ``chunk``: median time from the prologue's end to the last batch's chunk
   math being done; ``wcomp``: consumer warp 0's SM clock cycles (thousands)
-  inside the chunk math.
+  inside the chunk math.  For GatedDeltaNet stages ``pro`` is the time to the
+  head's inputs having arrived and ``chunk`` the state update after that; for
+  attention stages ``pro`` is the q / k / v preparation, ``chunk`` the
+  positions up to the published partials, ``wcomp`` the combine (us).
 
 Also prints the step time measured with CUDA events over ``--steps`` steps.
 """
@@ -50,6 +53,10 @@ def stage_names(cfg):
     return names
 
 
+def kinds_of(eng):
+    return [KINDS[st.kind] for st in eng.stages]
+
+
 def timeline(eng):
     """One step with the timeline on: [stages, grid, 10] int64 (stamps in ns from the earliest one)."""
     ns, grid = len(eng.stages), eng.grid
@@ -61,13 +68,24 @@ def timeline(eng):
     t = (buf.cpu().to(torch.int64) & 0xFFFFFFFF).view(ns, grid, NF)
     base = int(t[0, :, 0].min())
     t[:, :, :5] = (t[:, :, :5] - base) % (1 << 32)
-    for f in (7, 8):
+    kinds = kinds_of(eng)
+    for f in (7, 8, 9):
         nz = t[:, :, f] != 0
-        t[:, :, f] = torch.where(nz, (t[:, :, f] - base) % (1 << 32), torch.zeros_like(t[:, :, f]))
+        if f == 9:  # warp-0 cycles for GEMV stages, a stamp for attention stages
+            nz &= torch.tensor([k == "attn" for k in kinds]).view(-1, 1)
+        t[:, :, f] = torch.where(nz, (t[:, :, f] - base) % (1 << 32), t[:, :, f])
     return t
 
 
-def summarize(cfg, t):
+def _med_since(stamp, since):
+    """Median over the CTAs that recorded `stamp` (non-zero) of stamp - since."""
+    m = (stamp != 0) & (since != 0)
+    if not bool(m.any()):
+        return 0
+    return max(0, int((stamp[m] - since[m]).median()))
+
+
+def summarize(cfg, t, kinds=None):
     names = stage_names(cfg)
     rows = []
     prev_end = int(t[0, :, 0].min())
@@ -79,15 +97,16 @@ def summarize(cfg, t):
                          sync=int(start.median()) - prev_end, work_med=statistics.median(work), work_max=max(work),
                          lead=int(start.median()) - int(p1.median()),
                          pblk=int(t[s, :, 5].median()), cblk=int(t[s, :, 6].median()),
-                         pro=max(0, int((t[s, :, 7] - start).median())) if int(t[s, :, 7].max()) else 0,
-                         chunks=max(0, int((t[s, :, 8] - t[s, :, 7]).median())) if int(t[s, :, 8].max()) else 0,
-                         wcomp=int(t[s, :, 9].median())))
+                         pro=_med_since(t[s, :, 7], start),
+                         chunks=_med_since(t[s, :, 8], t[s, :, 7]),
+                         wcomp=int(t[s, :, 9].median()) if kinds is None or kinds[s] == "gemv" else
+                         _med_since(t[s, :, 9], t[s, :, 8])))
         prev_end = last_end
     return rows
 
 
-def report(cfg, t, per_stage=False, out=print):
-    rows = summarize(cfg, t)
+def report(cfg, t, per_stage=False, out=print, kinds=None):
+    rows = summarize(cfg, t, kinds)
     total = int(t[:, :, 2].max()) - int(t[0, :, 0].min())
     out(f"timeline step: {total / 1000:.1f} us")
     agg = {}
@@ -138,7 +157,7 @@ def main():
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / args.steps
     print(f"step: {ms * 1000:.1f} us ({1000 / ms:.1f} tok/s), {len(eng.stages)} stages, grid {eng.grid}")
-    report(cfg, timeline(eng), args.per_stage)
+    report(cfg, timeline(eng), args.per_stage, kinds=kinds_of(eng))
 
 
 if __name__ == "__main__":
