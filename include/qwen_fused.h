@@ -100,6 +100,11 @@ int qwen_last_error(void);
  * [0, max_seq), 6 a tensor-parallel peer exchange timed out, 7 a K-slice
  * count outside [1, max_slices]. */
 int qwen_get_device_error(unsigned int* out);
+/* Limit in ns of the waits on other CTAs or ranks (step-kernel stage
+ * counters, tensor-parallel peer flags): 1e6 .. 2e9, or 0 for the default
+ * 2e9.  A wait that runs out records its error code above and gives up; the
+ * launch returns and the context stays usable. */
+int qwen_set_wait_timeout_ns(unsigned long long ns);
 /* Enable (default) or disable programmatic dependent launch in the engine entry points. */
 void qwen_set_pdl(int enable);
 /* Up to four device regions (null / 0 ignored; 16-byte aligned) that the next

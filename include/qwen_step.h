@@ -146,9 +146,14 @@ int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_
 /* One launch of the whole program on `stream`. */
 int qwen_step_launch(void* program, cudaStream_t stream);
 
-/* Clears the program's stage counters and abort flag on `stream` (after an
- * abandoned step). */
+/* Clears the program's stage counters, abort flag, argmax and attention
+ * workspaces on `stream` (after an abandoned step). */
 int qwen_step_reset(void* program, cudaStream_t stream);
+
+/* Failure-detection hook: on the following launches CTA 0 does not report
+ * stage `stage` done (-1: off), so the next stage's grid-wide wait runs out
+ * (qwen_set_wait_timeout_ns) and the step is abandoned with device error 8. */
+int qwen_step_set_drop(void* program, int stage);
 
 int qwen_step_destroy(void* program);
 

@@ -31,12 +31,14 @@ F32 = torch.float32
 
 
 class OracleModel:
-    def __init__(self, cfg, weights, max_seq: int):
+    def __init__(self, cfg, weights, max_seq: int, device="cpu"):
         self.cfg = cfg
         self.w = weights
         self.max_seq = max_seq
+        self.dev = torch.device(device)  # where the caches live: the weights' device
         self.rotary_dim = int(cfg.head_dim * cfg.partial_rotary_factor)
-        self.cos, self.sin = ops.rope_tables(max_seq, self.rotary_dim, cfg.rope_theta)
+        cos, sin = ops.rope_tables(max_seq, self.rotary_dim, cfg.rope_theta)
+        self.cos, self.sin = cos.to(self.dev), sin.to(self.dev)
         self.reset()
 
     def reset(self):
@@ -48,12 +50,12 @@ class OracleModel:
         for i, lt in enumerate(cfg.layer_types):
             if lt == "full_attention":
                 shape = (cfg.num_key_value_heads, self.max_seq, cfg.head_dim)
-                self.k_cache[i] = torch.zeros(shape, dtype=BF16)
-                self.v_cache[i] = torch.zeros(shape, dtype=BF16)
+                self.k_cache[i] = torch.zeros(shape, dtype=BF16, device=self.dev)
+                self.v_cache[i] = torch.zeros(shape, dtype=BF16, device=self.dev)
             else:
-                self.conv[i] = torch.zeros(conv_dim, cfg.linear_conv_kernel_dim, dtype=BF16)
+                self.conv[i] = torch.zeros(conv_dim, cfg.linear_conv_kernel_dim, dtype=BF16, device=self.dev)
                 self.state[i] = torch.zeros(cfg.linear_num_value_heads, cfg.linear_key_head_dim,
-                                            cfg.linear_value_head_dim, dtype=F32)
+                                            cfg.linear_value_head_dim, dtype=F32, device=self.dev)
 
     # -- layers ------------------------------------------------------------
     def _full(self, h, ly, i):

@@ -48,8 +48,8 @@ def expand_scales(n_rows: int, k: int, scale: torch.Tensor, kblk: int) -> torch.
     ``(row/128)*K_blk + k/128``.
     """
     s = scale.to(F32)
-    kcols = torch.arange(k) // BLOCK
-    rows = torch.arange(n_rows)
+    kcols = torch.arange(k, device=s.device) // BLOCK
+    rows = torch.arange(n_rows, device=s.device)
     if kblk < 0:
         grid = s.reshape(n_rows, -kblk)[:, kcols]
     elif kblk == 1:

@@ -37,6 +37,16 @@ __device__ __forceinline__ void qwen_err_set(unsigned code) {
   atomicCAS(&g_qwen_err, 0u, code);
 }
 
+// Limit of the waits on other CTAs or ranks (step-kernel stage counters, p2p
+// flags), in ns; the host may lower it (qwen_set_wait_timeout_ns), e.g. for a
+// test that lets such a wait run out.  Waits on a CTA's own bulk copies keep
+// the fixed QWEN_WAIT_TIMEOUT_NS.
+__device__ unsigned long long g_qwen_wait_ns = QWEN_WAIT_TIMEOUT_NS;
+
+__device__ __forceinline__ unsigned long long qwen_wait_ns() {
+  return *reinterpret_cast<volatile unsigned long long*>(&g_qwen_wait_ns);
+}
+
 // ---------------------------------------------------------------------------
 // Conversions
 // ---------------------------------------------------------------------------

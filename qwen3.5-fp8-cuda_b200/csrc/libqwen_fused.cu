@@ -184,6 +184,12 @@ int qwen_last_error(void) {
   return e;
 }
 
+int qwen_set_wait_timeout_ns(unsigned long long ns) {
+  if (ns == 0) ns = QWEN_WAIT_TIMEOUT_NS;
+  if (ns < 1000000ull || ns > QWEN_WAIT_TIMEOUT_NS) return record(cudaErrorInvalidValue);
+  return record(cudaMemcpyToSymbol(g_qwen_wait_ns, &ns, sizeof(ns)));
+}
+
 int qwen_get_device_error(unsigned int* out) {
   unsigned int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_qwen_err, sizeof(v));

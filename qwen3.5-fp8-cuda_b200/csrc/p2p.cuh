@@ -72,9 +72,9 @@ __device__ __forceinline__ bool p2p_wait_all(const P2PTable& t, unsigned par, un
   const unsigned* f = t.flag[t.rank] + par * 8;
   for (int src = 0; src < t.world; ++src) {
     if (ld_acquire_sys_u32(f + src) >= want) continue;
-    const uint64_t t0 = globaltimer_ns();
+    const uint64_t t0 = globaltimer_ns(), lim = qwen_wait_ns();
     while (ld_acquire_sys_u32(f + src) < want)
-      if (globaltimer_ns() - t0 > QWEN_WAIT_TIMEOUT_NS) return false;
+      if (globaltimer_ns() - t0 > lim) return false;
   }
   return true;
 }

@@ -157,6 +157,7 @@ struct StProgram {
   unsigned* abort_flag;  // set by a timed-out wait; every wait then gives up at once
   unsigned* timeline;    // optional [nstages][grid][ST_TL]: %globaltimer (low 32 bits, ns) per stage and CTA
   const int* pos;        // decode position read by the attention stages (constant within a step), or null
+  int drop_stage;        // test hook: CTA 0 does not report stage drop_stage done (-1: off)
 };
 
 // Timeline fields of one (stage, CTA): the consumers' wait for the previous
@@ -200,13 +201,13 @@ __device__ __forceinline__ void st_abort(unsigned* abort_flag) {
 // mbarrier phase wait, bounded by QWEN_WAIT_TIMEOUT_NS and by the abort flag.
 __device__ __forceinline__ bool st_mbar_wait(uint32_t bar, uint32_t parity, unsigned* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const uint64_t t0 = globaltimer_ns(), lim = qwen_wait_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 16; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (st_aborted(abort_flag)) return false;
-    if (globaltimer_ns() - t0 > QWEN_WAIT_TIMEOUT_NS) {
+    if (globaltimer_ns() - t0 > lim) {
       st_abort(abort_flag);
       return false;
     }
@@ -216,13 +217,13 @@ __device__ __forceinline__ bool st_mbar_wait(uint32_t bar, uint32_t parity, unsi
 // Wait until `count` CTAs have arrived at `counter` (acquire, GPU scope).
 __device__ __forceinline__ bool st_wait_count(const unsigned* counter, unsigned count, unsigned* abort_flag) {
   if (ld_acquire_gpu_u32(counter) >= count) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const uint64_t t0 = globaltimer_ns(), lim = qwen_wait_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 8; ++i)
       if (ld_acquire_gpu_u32(counter) >= count) return true;
     if (st_aborted(abort_flag)) return false;
-    if (globaltimer_ns() - t0 > QWEN_WAIT_TIMEOUT_NS) {
+    if (globaltimer_ns() - t0 > lim) {
       st_abort(abort_flag);
       return false;
     }
@@ -936,7 +937,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     if (tid == 0) {
       st_stamp(P, s, ST_TL_END);
       __threadfence();
-      atomicAdd(P.counters + s, 1u);
+      if (s != P.drop_stage || blockIdx.x != 0) atomicAdd(P.counters + s, 1u);
     }
   }
   // End of the step: the last CTA clears the counters for the next launch

@@ -9,6 +9,7 @@
 
 #include <cmath>
 #include <cstdlib>
+#include <utility>
 #include <vector>
 
 namespace {
@@ -21,6 +22,10 @@ struct StepProgramHost {
   unsigned* d_counters = nullptr;  // nstages + 1 counters, then the abort flag
   unsigned* timeline = nullptr;    // optional per-stage timestamps (qwen_step_set_timeline)
   const int* pos = nullptr;        // the attention stages' position (all of them share one)
+  int drop_stage = -1;             // test hook (qwen_step_set_drop)
+  // workspaces a completed step leaves zeroed and an abandoned one may not:
+  // ARGMAX {key, count} words and attention split counters (cleared by reset)
+  std::vector<std::pair<void*, size_t>> scratch;
 };
 
 bool g_step_attr_done[64] = {};
@@ -296,6 +301,11 @@ int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_
   p->pos = pos;
   p->grid = grid;
   p->nstages = nstages;
+  for (int i = 0; i < nstages; ++i) {
+    const qwen_step_stage& st = stages[i];
+    if (st.kind == QWEN_STEP_GEMV && st.am_ws) p->scratch.emplace_back(st.am_ws, 2 * sizeof(unsigned long long));
+    if (st.kind == QWEN_STEP_ATTN && st.a_cnt) p->scratch.emplace_back(st.a_cnt, sizeof(unsigned) * st.a_kv);
+  }
   e = cudaMalloc(&p->d_stages, sizeof(qwen::StStage) * nstages);
   if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, sizeof(unsigned) * (nstages + 2));
   if (e == cudaSuccess)
@@ -321,6 +331,7 @@ int qwen_step_launch(void* program, cudaStream_t stream) {
   P.abort_flag = p->d_counters + p->nstages + 1;
   P.timeline = p->timeline;
   P.pos = p->pos;
+  P.drop_stage = p->drop_stage;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p->grid);
   cfg.blockDim = dim3(qwen::ST_THREADS);
@@ -337,7 +348,17 @@ int qwen_step_launch(void* program, cudaStream_t stream) {
 int qwen_step_reset(void* program, cudaStream_t stream) {
   StepProgramHost* p = static_cast<StepProgramHost*>(program);
   if (!p) return record(cudaErrorInvalidValue);
-  return record(cudaMemsetAsync(p->d_counters, 0, sizeof(unsigned) * (p->nstages + 2), stream));
+  cudaError_t e = cudaMemsetAsync(p->d_counters, 0, sizeof(unsigned) * (p->nstages + 2), stream);
+  for (size_t i = 0; i < p->scratch.size() && e == cudaSuccess; ++i)
+    e = cudaMemsetAsync(p->scratch[i].first, 0, p->scratch[i].second, stream);
+  return record(e);
+}
+
+int qwen_step_set_drop(void* program, int stage) {
+  StepProgramHost* p = static_cast<StepProgramHost*>(program);
+  if (!p || stage < -1 || stage >= p->nstages) return record(cudaErrorInvalidValue);
+  p->drop_stage = stage;
+  return 0;
 }
 
 int qwen_step_destroy(void* program) {

@@ -50,6 +50,7 @@ REFERENCE_FP8_ARGTYPES = {
 NEW_FUSED = {
     "qwen_last_error": (I, []),
     "qwen_get_device_error": (I, [P]),
+    "qwen_set_wait_timeout_ns": (I, [ctypes.c_ulonglong]),
     "qwen_set_pdl": (None, [I]),
     "qwen_set_prefetch": (None, [P, ctypes.c_ulonglong, P, ctypes.c_ulonglong, P, ctypes.c_ulonglong, P,
                                  ctypes.c_ulonglong]),
@@ -89,6 +90,7 @@ NEW_FUSED = {
     "qwen_step_create": (I, [P, I, P]),
     "qwen_step_launch": (I, [P, P]),
     "qwen_step_reset": (I, [P, P]),
+    "qwen_step_set_drop": (I, [P, I]),
     "qwen_step_destroy": (I, [P]),
     "qwen_step_set_timeline": (I, [P, P]),
     "qwen_step_grid": (I, [P]),

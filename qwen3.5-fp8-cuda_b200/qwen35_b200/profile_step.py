@@ -62,7 +62,7 @@ def timeline(eng):
     ns, grid = len(eng.stages), eng.grid
     buf = torch.zeros(ns * grid * NF, dtype=torch.int32, device=eng.device)
     eng.lib.qwen_step_set_timeline(eng.prog, ctypes.c_void_p(buf.data_ptr()))
-    eng.step()
+    eng.step_eager()  # a captured graph holds the launch parameters it was captured with
     torch.cuda.synchronize(eng.device)
     eng.lib.qwen_step_set_timeline(eng.prog, ctypes.c_void_p(0))
     t = (buf.cpu().to(torch.int64) & 0xFFFFFFFF).view(ns, grid, NF)

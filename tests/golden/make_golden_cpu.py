@@ -167,7 +167,9 @@ def load_with_reference(Eng, ckpt_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("QWEN_REFERENCE_ROOT")
+                    or os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), "reference"),
+                    help="reference checkout (default: $QWEN_REFERENCE_ROOT, else 'reference' beside the repository)")
     ap.add_argument("--out", default=os.path.join(HERE, "cpu_golden.safetensors"))
     args = ap.parse_args()
     ref = load_reference(args.ref)

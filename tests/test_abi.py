@@ -87,7 +87,8 @@ def test_headers_compile_as_c(header, tmp_path):
     assert r.returncode == 0, r.stderr
 
 
-REF_MAIN = "/root/reference/main.py"
+REF_ROOT = os.environ.get("QWEN_REFERENCE_ROOT") or os.path.join(os.path.dirname(REPO), "reference")
+REF_MAIN = os.path.join(REF_ROOT, "main.py")
 
 
 @pytest.mark.skipif(not os.path.exists(REF_MAIN), reason="reference checkout not present")
