@@ -571,6 +571,19 @@ def run_ours(args):
                              "(248320x2560 E4M3, config 2)", "achieved": round(head_gbs, 1), "unit": "GB/s",
                    "frac": round(head_gbs / peak, 4), "bytes_per_launch": hb, "us_per_launch": round(head_s * 1e6, 2),
                    "traffic": load_traffic()}
+    head_stage = None
+    if step_engine:
+        # config 2 on the step kernel, E4M3 and BF16 heads (one-stage programs)
+        try:
+            from qwen35_b200.profile_step import head_stage_rate
+            head_stage = {"unit": "GB/s of algorithmic bytes (weights, scales, x); frac of the measured peak",
+                          "shape": "248320x2560, x BF16, fused greedy argmax, one step-kernel launch per GEMV"}
+            for name, fp8 in (("e4m3", True), ("bf16", False)):
+                r = head_stage_rate(fp8=fp8)
+                r["frac"] = round(r["gbs"] / peak, 4)
+                head_stage[name] = r
+        except Exception as exc:  # reported, never allowed to drop the line
+            head_stage = {"error": repr(exc)[:200]}
     if step_engine:
         # the dominant (only) kernel of a step: the persistent step kernel; one
         # launch per step, so its launch time is the device time per step
@@ -604,6 +617,7 @@ def run_ours(args):
         "step_roofline": {"bytes_per_step": sbytes, "achieved": round(step_gbs, 1),
                           "frac": round(step_gbs / peak, 4), "unit": "GB/s"},
         "lm_head_kernel": head_kernel,
+        "lm_head_step_stage": head_stage,
         "clocks": clocks,
         "pdl": not args.no_pdl,
     }

@@ -129,6 +129,9 @@ typedef struct qwen_step_stage {
   float* a_ws;           /* FP32 [heads][nsplit][dim + 2] */
   unsigned* a_cnt;       /* [kv] zeroed counters (left zeroed) */
   void* a_out;           /* BF16 [heads][dim] */
+  /* GEMV with BF16 weights (packed by qwen_step_pack_bf16; one STORE / ARGMAX /
+     SLICES segment, K a multiple of 256): x is used as BF16, no block scales */
+  int wbf16;
 } qwen_step_stage;
 
 /* Bytes of a packed [N, K] matrix: ceil(N/32) * (K/512) * 16400 (0 if K % 512). */
@@ -138,6 +141,12 @@ size_t qwen_step_packed_bytes(int N, int K);
  * BF16, or FP32 with scale_f32 = 1) for GEMV stages.  K_blk must be K/128. */
 int qwen_step_pack(const void* w, const void* s, int scale_f32, int N, int K, int K_blk, void* out,
                    cudaStream_t stream);
+
+/* BF16 weights w [N, K] for a GEMV stage with wbf16 = 1: chunks of 32 rows x
+ * 256 K (16 KB, each lane's m16n8k16 A fragments contiguous) + 16 zero bytes;
+ * ceil(N/32) * (K/256) * 16400 bytes (0 if K % 256). */
+size_t qwen_step_packed_bytes_bf16(int N, int K);
+int qwen_step_pack_bf16(const void* w, int N, int K, void* out, cudaStream_t stream);
 
 /* Builds a program from `nstages` stage descriptions (copied; the pointers
  * they hold must stay valid while the program is used) on the current device. */

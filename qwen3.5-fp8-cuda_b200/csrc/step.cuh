@@ -130,6 +130,8 @@ struct alignas(16) StStage {
   // attention: one unit per (KV head, split)
   AttnArgs attn;
   int attn_dim, attn_g;
+  int wbf16;           // GEMV: BF16 weights (chunks of 32 rows x 256 K), x kept as BF16
+  int pad_[3];
 };
 
 // Shared memory plan (bytes from the dynamic shared memory base).
@@ -492,6 +494,15 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
     const int b = warp + i * ST_CW;
     if (b >= nb) continue;  // warp-uniform
     const int k0 = b * 128 + lane * 4;
+    if (S.wbf16) {  // BF16 weights: x stays BF16 (xh holds K BF16 values)
+      const __nv_bfloat162 p01 = __floats2bfloat162_rn(v[i][0], v[i][1]);
+      const __nv_bfloat162 p23 = __floats2bfloat162_rn(v[i][2], v[i][3]);
+      uint2 pv;
+      pv.x = *reinterpret_cast<const uint32_t*>(&p01);
+      pv.y = *reinterpret_cast<const uint32_t*>(&p23);
+      *reinterpret_cast<uint2*>(xh + 2 * k0) = pv;
+      continue;
+    }
     const float x[4] = {v[i][0], v[i][1], v[i][2], v[i][3]};
     const float m = mx[i];
     // m = 1.f * 2^(ebits - 127): e = 134 - ebits puts m * 2^e in [2^7, 2^8)
@@ -567,6 +578,40 @@ __device__ __forceinline__ void st_chunk(const uint8_t* base, const uint8_t* xh,
     a0 = fmaf(f[kb], d[kb][0] + d[kb][1] * 0.03125f, a0);
     a1 = fmaf(f[kb], d[kb][2] + d[kb][3] * 0.03125f, a1);
   }
+}
+
+// BF16 MMA D (16x8 f32) = A (16x16 BF16) x B (16x8 BF16) + D.
+__device__ __forceinline__ void st_mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 16-row group (rg) of a BF16 chunk (32 rows x 256 K) on one warp: the
+// chunk holds, per group and 16-K step j, each lane's A fragment as 16
+// contiguous bytes; x (BF16) is the B operand's column 0 (lanes 0-3), so
+// lanes with lane % 4 == 0 end with the FP32 sums of rows 16 rg + lane / 4
+// (a0) and + 8 (a1).  Four independent accumulator chains.
+__device__ __forceinline__ void st_chunk_bf16(const uint8_t* base, const bf16* xs, int c, int rg, int lane, float& a0,
+                                              float& a1) {
+  const uint8_t* wl = base + rg * (ST_WBYTES / 2) + lane * 16;
+  const bf16* xc = xs + c * 256 + 2 * (lane & 3);
+  float d[4][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint4 w = *reinterpret_cast<const uint4*>(wl + j * 512);
+    uint32_t b0 = 0u, b1 = 0u;
+    if (lane < 4) {
+      b0 = *reinterpret_cast<const uint32_t*>(xc + 16 * j);
+      b1 = *reinterpret_cast<const uint32_t*>(xc + 16 * j + 8);
+    }
+    st_mma_bf16(d[j & 3], w.x, w.y, w.z, w.w, b0, b1);
+  }
+  a0 = (d[0][0] + d[1][0]) + (d[2][0] + d[3][0]);
+  a1 = (d[0][2] + d[1][2]) + (d[2][2] + d[3][2]);
 }
 
 // CTA-wide max of the running argmax keys, the cross-CTA maximum and its
@@ -653,7 +698,10 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
       const int c = sl * per + (pair ? (i >> 1) : i);
       float a0, a1;
       const long long tc = X.timeline ? clock64() : 0;
-      st_chunk(X.ring + slot * ST_CHUNK, X.xh, X.xl, X.xinv, c, rg, lane, a0, a1);
+      if (S.wbf16)
+        st_chunk_bf16(X.ring + slot * ST_CHUNK, reinterpret_cast<const bf16*>(X.xh), c, rg, lane, a0, a1);
+      else
+        st_chunk(X.ring + slot * ST_CHUNK, X.xh, X.xl, X.xinv, c, rg, lane, a0, a1);
       if (X.timeline) comp += (uint64_t)(clock64() - tc);
       __syncwarp();
       if (lane == 0) mbar_arrive(X.empty0 + 8 * slot);  // one of the pair's two arrivals
@@ -987,6 +1035,32 @@ __global__ void step_pack_kernel(const uint8_t* __restrict__ w, const void* __re
       for (int i = 0; i < 4; ++i) f[i] = load_scale<ST>(s, rb * kblk + c * 4 + i);
       *reinterpret_cast<float4*>(dst + ST_WBYTES) = make_float4(f[0], f[1], f[2], f[3]);
     }
+  }
+}
+
+// BF16 weights [N, K] -> chunks of 32 rows x 256 K: chunk (t, c) holds, for
+// row group rg = 0, 1, K step j = 0..15 and lane, the 16 bytes of the lane's
+// m16n8k16 A fragment: W[r][k .. k+1], W[r+8][k .. k+1], W[r][k+8 .. k+9],
+// W[r+8][k+8 .. k+9] with r = 32t + 16rg + lane/4, k = 256c + 16j + 2(lane%4),
+// then 16 zero bytes.  Rows past N are zero.  One thread per 4 bytes.
+__global__ void step_pack_bf16_kernel(const bf16* __restrict__ w, int N, int K, uint8_t* __restrict__ out) {
+  const int C = K / 256;
+  const long long tiles = (N + ST_ROWS - 1) / ST_ROWS;
+  constexpr int WORDS = ST_CHUNK / 4;
+  const long long total = tiles * C * WORDS;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long chunk = idx / WORDS;
+    const int p = (int)(idx - chunk * WORDS);
+    const int t = (int)(chunk / C), c = (int)(chunk - (long long)t * C);
+    uint32_t v = 0u;
+    if (p < ST_WBYTES / 4) {
+      const int rg = p >> 11, j = (p >> 7) & 15, lane = (p >> 2) & 31, reg = p & 3;
+      const int row = t * ST_ROWS + 16 * rg + (lane >> 2) + ((reg & 1) ? 8 : 0);
+      const int k = c * 256 + 16 * j + 2 * (lane & 3) + ((reg & 2) ? 8 : 0);
+      if (row < N) v = *reinterpret_cast<const uint32_t*>(w + (size_t)row * K + k);
+    }
+    reinterpret_cast<uint32_t*>(out + chunk * ST_CHUNK)[p] = v;
   }
 }
 

@@ -76,6 +76,8 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
   if (in.kind == QWEN_STEP_GEMV) {
     if (in.K <= 0 || in.K % ST_KC || in.K > ST_MAXK || in.nseg < 1 || in.nseg > ST_MAX_SEG)
       return cudaErrorInvalidValue;
+    // BF16 weights: one segment, K a multiple of 256 that the BF16 x buffer holds
+    if (in.wbf16 && (in.nseg != 1 || in.pair || in.K % 256 || in.K > ST_MAXK / 2)) return cudaErrorInvalidValue;
     if (in.pro < QWEN_STEP_PRO_PLAIN || in.pro > QWEN_STEP_PRO_SLICES_NORM) return cudaErrorInvalidValue;
     if (in.pro != QWEN_STEP_PRO_SLICES_NORM && !in.x) return cudaErrorInvalidValue;
     if (in.pro != QWEN_STEP_PRO_PLAIN && (!in.norm_w || in.K > ST_NORM_MAXK)) return cudaErrorInvalidValue;
@@ -83,7 +85,8 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     if (in.pro == QWEN_STEP_PRO_SLICES_NORM && (!in.res || !in.sl_in || in.sl_stride < in.K))
       return cudaErrorInvalidValue;
     o.K = in.K;
-    o.C = in.K / ST_KC;
+    o.wbf16 = in.wbf16 ? 1 : 0;
+    o.C = in.K / (o.wbf16 ? 256 : ST_KC);
     o.pro = in.pro;
     o.nseg = in.nseg;
     o.pair = in.pair ? 1 : 0;
@@ -244,6 +247,22 @@ extern "C" {
 size_t qwen_step_packed_bytes(int N, int K) {
   if (N <= 0 || K <= 0 || K % qwen::ST_KC) return 0;
   return (size_t)((N + qwen::ST_ROWS - 1) / qwen::ST_ROWS) * (size_t)(K / qwen::ST_KC) * qwen::ST_CHUNK;
+}
+
+size_t qwen_step_packed_bytes_bf16(int N, int K) {
+  if (N <= 0 || K <= 0 || K % 256) return 0;
+  return (size_t)((N + qwen::ST_ROWS - 1) / qwen::ST_ROWS) * (size_t)(K / 256) * qwen::ST_CHUNK;
+}
+
+int qwen_step_pack_bf16(const void* w, int N, int K, void* out, cudaStream_t stream) {
+  if (!w || !out || N <= 0 || K <= 0 || K % 256) return record(cudaErrorInvalidValue);
+  const long long words = (long long)((N + qwen::ST_ROWS - 1) / qwen::ST_ROWS) * (K / 256) * (qwen::ST_CHUNK / 4);
+  const int block = 256;
+  const long long want = (words + block - 1) / block;
+  const int grid = (int)(want < 65535 ? want : 65535);
+  qwen::step_pack_bf16_kernel<<<grid, block, 0, stream>>>(static_cast<const qwen::bf16*>(w), N, K,
+                                                          static_cast<uint8_t*>(out));
+  return record(cudaGetLastError());
 }
 
 int qwen_step_pack(const void* w, const void* s, int scale_f32, int N, int K, int K_blk, void* out,

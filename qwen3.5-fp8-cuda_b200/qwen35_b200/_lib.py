@@ -90,6 +90,8 @@ NEW_FUSED = {
     "qwen_step_create": (I, [P, I, P]),
     "qwen_step_launch": (I, [P, P]),
     "qwen_step_reset": (I, [P, P]),
+    "qwen_step_packed_bytes_bf16": (ctypes.c_size_t, [I, I]),
+    "qwen_step_pack_bf16": (I, [P, I, I, P, P]),
     "qwen_step_set_drop": (I, [P, I]),
     "qwen_step_destroy": (I, [P]),
     "qwen_step_set_timeline": (I, [P, P]),

@@ -131,6 +131,55 @@ def report(cfg, t, per_stage=False, out=print, kinds=None):
     return rows
 
 
+def head_stage_rate(fp8: bool = True, reps: int = 20, seed: int = 12):
+    """Config 2 on the step kernel: a one-stage program (x given, fused argmax)
+    over the 248320 x 2560 LM head, E4M3 with 128 x 128 block scales or BF16
+    (N(0, 0.02)).  Returns {us_per_launch, bytes_per_launch, gbs}: algorithmic
+    bytes (weights, scales, x) over the CUDA-event time of `reps` launches."""
+    import ctypes as C
+    from . import _lib
+    from .step import EPI_ARGMAX, GEMV, PRO_PLAIN, StepSeg, StepStage, create_program, pack_linear, pack_linear_bf16
+    V, H = 248320, 2560
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(H, generator=g, device="cuda").to(torch.bfloat16)
+    if fp8:
+        from .weights import _fp8
+        w, sc = _fp8(V, H, g, "cuda")
+        packed = pack_linear(w, sc)
+        nbytes = w.numel() + sc.numel() * sc.element_size() + 2 * H
+        del w
+    else:
+        w = (torch.randn(V, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        packed = pack_linear_bf16(w)
+        nbytes = w.numel() * 2 + 2 * H
+        del w
+    am_ws = torch.zeros(2, dtype=torch.int64, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    tok = torch.zeros(1, dtype=torch.int64, device="cuda")
+    seg = StepSeg()
+    seg.w, seg.n, seg.epi = packed.data_ptr(), V, EPI_ARGMAX
+    st = StepStage()
+    st.kind, st.K, st.pro, st.nseg, st.wbf16 = GEMV, H, PRO_PLAIN, 1, 0 if fp8 else 1
+    st.x = x.data_ptr()
+    st.seg[0] = seg
+    st.am_ws, st.am_key_out, st.am_token_out = am_ws.data_ptr(), key.data_ptr(), tok.data_ptr()
+    prog = create_program([st])
+    lib = _lib.fused()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        _lib.check(lib.qwen_step_launch(prog, stream), "qwen_step_launch")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        _lib.check(lib.qwen_step_launch(prog, stream), "qwen_step_launch")
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    lib.qwen_step_destroy(prog)
+    return {"us_per_launch": round(us, 2), "bytes_per_launch": nbytes, "gbs": round(nbytes / us / 1e3, 1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=32)

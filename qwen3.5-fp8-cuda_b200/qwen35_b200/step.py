@@ -62,6 +62,7 @@ class StepStage(ctypes.Structure):
         ("a_heads", ctypes.c_int), ("a_kv", ctypes.c_int), ("a_dim", ctypes.c_int), ("a_rot", ctypes.c_int),
         ("a_eps", ctypes.c_float), ("a_chunk", ctypes.c_int), ("a_nsplit", ctypes.c_int), ("a_ws", P),
         ("a_cnt", P), ("a_out", P),
+        ("wbf16", ctypes.c_int),
     ]
 
 
@@ -82,6 +83,21 @@ def pack_linear(w_u8: torch.Tensor, scale: torch.Tensor, stream=None) -> torch.T
     st = P(stream if stream is not None else torch.cuda.current_stream(w_u8.device).cuda_stream)
     _lib.check(lib.qwen_step_pack(P(w_u8.data_ptr()), P(scale.data_ptr()), 1 if scale.dtype == torch.float32 else 0,
                                   n, k, kblk, P(out.data_ptr()), st), "qwen_step_pack")
+    return out
+
+
+def pack_linear_bf16(w_bf16: torch.Tensor, stream=None) -> torch.Tensor:
+    """Pack a device [N, K] BF16 weight for a ``wbf16`` GEMV stage
+    (``qwen_step_pack_bf16``); returns the packed bytes (uint8, device)."""
+    lib = _lib.fused()
+    n, k = w_bf16.shape
+    nbytes = lib.qwen_step_packed_bytes_bf16(n, k)
+    if nbytes == 0 or w_bf16.dtype != torch.bfloat16:
+        raise ValueError(f"BF16 step GEMV needs a BF16 weight with K % 256 == 0 (N={n}, K={k})")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=w_bf16.device)
+    st = P(stream if stream is not None else torch.cuda.current_stream(w_bf16.device).cuda_stream)
+    _lib.check(lib.qwen_step_pack_bf16(P(w_bf16.contiguous().data_ptr()), n, k, P(out.data_ptr()), st),
+               "qwen_step_pack_bf16")
     return out
 
 
@@ -129,13 +145,14 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
                 if key in ly:
                     mats.append(ly[key])
         for m in mats:
-            if not isinstance(m, tuple):
-                raise NotImplementedError("BF16 LM head: the step kernel streams block-FP8 weights")
-            self.packed[m[0].data_ptr()] = pack_linear(m[0], m[1])
+            if isinstance(m, tuple):
+                self.packed[m[0].data_ptr()] = pack_linear(m[0], m[1])
+            else:  # BF16 LM head (the reference's F.linear head, main.py:1600-1601)
+                self.packed[m.data_ptr()] = pack_linear_bf16(m)
         torch.cuda.synchronize(self.device)
 
     def _pk(self, m):
-        return self.packed[m[0].data_ptr()].data_ptr()
+        return self.packed[(m[0] if isinstance(m, tuple) else m).data_ptr()].data_ptr()
 
     def _gemv(self, K, pro, segs, x=None, res=None, norm_w=None, h_out=None, pair=0, sl_out=False, nslice=0):
         st = StepStage()
@@ -168,7 +185,7 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
         s = StepSeg()
         s.w = self._pk(m)
         s.w2 = None if w2 is None else self._pk(w2)
-        s.n = m[0].shape[0]
+        s.n = (m[0] if isinstance(m, tuple) else m).shape[0]
         s.epi = epi
         s.y = _p(y)
         s.aux0 = _p(aux0)
@@ -253,6 +270,7 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
                                      sl_out=True, nslice=self.nslice))
         head = self._gemv(H, PRO_SLICES_NORM, [self._seg(w["lm_head"], EPI_ARGMAX, y=self.logits)], res=self.h2,
                           h_out=self.hidden, norm_w=w["norm_f"])
+        head.wbf16 = 0 if isinstance(w["lm_head"], tuple) else 1
         head.am_ws = self.am_ws.data_ptr()
         head.am_key_out = self.key.data_ptr()
         head.am_token_out = self.token.data_ptr()

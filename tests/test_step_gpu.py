@@ -12,6 +12,7 @@
 """
 
 import ctypes
+import math
 
 import pytest
 import torch
@@ -152,19 +153,56 @@ def test_slices_then_norm_pair(st, nslice):
     lib.fused().qwen_step_destroy(prog)
 
 
-def _tiny(seed=0, max_seq=96):
+def test_bf16_lm_head_stage_config2(st):
+    """BASELINE config 2's BF16 variant: the 248320 x 2560 BF16 LM head
+    (W ~ N(0, 0.02), x ~ N(0, 1)) with the fused greedy argmax, against an
+    FP32 torch reference of F.linear (main.py:1600-1601).  Every logit is a
+    correct BF16 rounding of the FP32 value; the token is the first-index
+    argmax of the kernel's own logits, and the reference's argmax unless the
+    two tokens' reference logits are within one BF16 ulp (FP32 summation
+    order may then round them either way)."""
+    lib, step = st
+    V, H = 248320, 2560
+    g = torch.Generator(device="cuda").manual_seed(12)
+    w = (torch.randn(V, H, generator=g, device="cuda") * 0.02).to(BF16)
+    x = torch.randn(H, generator=g, device="cuda").to(BF16)
+    packed = step.pack_linear_bf16(w)
+    logits = torch.empty(V, dtype=BF16, device="cuda")
+    am_ws = torch.zeros(2, dtype=torch.int64, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    token = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+    stg = step.StepStage()
+    stg.kind, stg.K, stg.pro, stg.nseg, stg.wbf16 = step.GEMV, H, step.PRO_PLAIN, 1, 1
+    stg.x = x.data_ptr()
+    stg.seg[0] = _seg(step, packed, V, step.EPI_ARGMAX, y=logits)
+    stg.am_ws, stg.am_key_out, stg.am_token_out = am_ws.data_ptr(), key.data_ptr(), token.data_ptr()
+    prog = _run_program(step, lib, [stg])
+    ref = torch.mv(w.float(), x.float())
+    assert_rounded(logits.float().cpu(), ref.cpu(), what="bf16 lm head")
+    tok = int(token.item())
+    assert tok == int(torch.argmax(logits.float()))
+    ref_b = ref.to(BF16).float()
+    rt = int(torch.argmax(ref_b))
+    if tok != rt:
+        ulp = 2.0 ** (math.floor(math.log2(abs(float(ref_b[rt])))) - 7)
+        assert float(ref[rt] - ref[tok]) <= ulp, (tok, rt)
+    lib.fused().qwen_step_destroy(prog)
+
+
+def _tiny(seed=0, max_seq=96, **kw):
     from qwen35_b200.config import qwen35_tiny
     from qwen35_b200.step import Qwen35StepEngine
     from qwen35_b200.weights import random_weights, to_device
-    cfg = qwen35_tiny()
+    cfg = qwen35_tiny(**kw)
     w_cpu = random_weights(cfg, seed=seed, device="cpu")
     eng = Qwen35StepEngine(cfg, to_device(w_cpu, "cuda"), max_seq=max_seq, keep_logits=True)
     return cfg, w_cpu, eng
 
 
-def test_tiny_model_step_kernel_follows_oracle():
+@pytest.mark.parametrize("fp8_head", [True, False])
+def test_tiny_model_step_kernel_follows_oracle(fp8_head):
     from qwen35_b200 import _lib
-    cfg, w_cpu, eng = _tiny()
+    cfg, w_cpu, eng = _tiny(fp8_lm_head=fp8_head)
     orc = OracleModel(cfg, w_cpu, max_seq=eng.max_seq)
     prompt = [int(t) for t in torch.randint(0, cfg.vocab_size, (8,), generator=torch.Generator().manual_seed(3))]
     tok = prompt[0]
