@@ -47,6 +47,15 @@ __device__ __forceinline__ unsigned long long qwen_wait_ns() {
   return *reinterpret_cast<volatile unsigned long long*>(&g_qwen_wait_ns);
 }
 
+// 16-byte global load through the read-only path without L1 allocation
+// (streamed weights: each byte is read once).
+__device__ __forceinline__ uint4 ld_nc_na_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // Conversions
 // ---------------------------------------------------------------------------

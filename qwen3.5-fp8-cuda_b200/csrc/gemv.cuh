@@ -722,6 +722,102 @@ __global__ void __launch_bounds__(GEMV_THREADS, GEMV_CTAS_PER_SM) gemv_mma_kerne
 // memory in 4-byte words (any K % 8 == 0, rows 4-byte aligned), FP32 x in
 // shared memory.  Used for shapes the row-streaming kernel does not cover.
 // ---------------------------------------------------------------------------
+// Direct-load GEMV for plain-x launches (the reference ABI's
+// launch_gemv_v4_extern and its grouped forms): one warp per output row, the
+// whole row's weights loaded at once (lane l holds K bytes [16 l + 512 j,
+// +16) for j < J, K = 512 J) before x is even read, so a launch puts every
+// weight byte it needs in flight in one wave and pays one memory latency.
+// The weights are static, so the loads are issued before
+// griddepcontrol.wait; x (BF16) is then staged in shared memory as FP32.
+// Per lane and j the 16 products are summed in FP32 and scaled once by the
+// row's scale of that 128-wide K block; the warp sum is the row's value.
+// Restates gemv_v4_kernel (fused_kernels.cu:91-151) with the same FP32
+// accumulation (a different summation order).
+template <typename ST, int J>
+__global__ void __launch_bounds__(256) gemv_direct_kernel(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int K = 512 * J;
+  float* xf = reinterpret_cast<float*>(smem);
+  unsigned long long* misc = reinterpret_cast<unsigned long long*>(smem + 4 * K);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  int total = 0;
+  for (int s = 0; s < a.nseg; ++s) total += a.seg[s].n;
+  int gr = blockIdx.x * nw + warp;
+  // the first row's weights and scales before anything else
+  uint4 wv[J];
+  float sc[J];
+  auto issue = [&](int row_g, int& si, int& r) {
+    si = 0;
+    r = row_g;
+    while (r >= a.seg[si].n) {
+      r -= a.seg[si].n;
+      ++si;
+    }
+    const GemvSeg& sg = a.seg[si];
+    const uint8_t* wr = sg.w + (size_t)r * K + lane * 16;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      wv[j] = ld_nc_na_v4(wr + 512 * j);
+      sc[j] = load_scale<ST>(sg.s, scale_index(sg.kblk, r, (lane * 16 + 512 * j) >> 7));
+    }
+  };
+  int si = 0, r = 0;
+  if (gr < total) issue(gr, si, r);
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
+  {  // x: every load issued before any is used (one round trip)
+    constexpr int XI = (K / 8 + 255) / 256;
+    uint4 xv[XI];
+#pragma unroll
+    for (int t = 0; t < XI; ++t) {
+      const int i = threadIdx.x + 256 * t;
+      if (i < K / 8) xv[t] = __ldg(reinterpret_cast<const uint4*>(a.x) + i);
+    }
+    // lane-interleaved: the 4 elements x[512 j + 16 l + 4 q, +4) live in
+    // float4 slot (4 j + q) * 32 + l, so lane l's reads below are
+    // consecutive 16-byte words across the warp (no bank conflicts)
+    float4* xf4 = reinterpret_cast<float4*>(xf);
+#pragma unroll
+    for (int t = 0; t < XI; ++t) {
+      const int i = threadIdx.x + 256 * t;
+      if (i >= K / 8) continue;
+      const uint32_t* vw = reinterpret_cast<const uint32_t*>(&xv[t]);
+      const int k0 = 8 * i, j = k0 >> 9, l = (k0 & 511) >> 4, q = (k0 & 15) >> 2;  // q even
+      const float2 f0 = bf2x_to_f2(vw[0]), f1 = bf2x_to_f2(vw[1]), f2 = bf2x_to_f2(vw[2]), f3 = bf2x_to_f2(vw[3]);
+      xf4[(4 * j + q) * 32 + l] = make_float4(f0.x, f0.y, f1.x, f1.y);
+      xf4[(4 * j + q + 1) * 32 + l] = make_float4(f2.x, f2.y, f3.x, f3.y);
+    }
+  }
+  __syncthreads();
+  unsigned long long am_best = 0ull;
+  while (gr < total) {
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const float4* x4 = reinterpret_cast<const float4*>(xf) + (4 * j) * 32 + lane;
+      const uint32_t* wq = reinterpret_cast<const uint32_t*>(&wv[j]);
+      float p = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f0 = h2u_to_f2(e4m3x2_to_f16x2(wq[q])), f1 = h2u_to_f2(e4m3x2_to_f16x2(wq[q] >> 16));
+        const float4 xv = x4[q * 32];
+        p = fmaf(xv.x, f0.x, p);
+        p = fmaf(xv.y, f0.y, p);
+        p = fmaf(xv.z, f1.x, p);
+        p = fmaf(xv.w, f1.y, p);
+      }
+      sum = fmaf(p, sc[j], sum);
+    }
+    sum = warp_sum(sum);
+    const GemvSeg& sg = a.seg[si];
+    const int rr = r;
+    gr += gridDim.x * nw;
+    if (gr < total) issue(gr, si, r);  // the next row's loads go out before this row's store
+    if (lane == 0) am_best = gemv_epilogue(sg, rr, sum, 0.f, am_best);
+  }
+  if (a.am_ws) argmax_finish(a, am_best, misc + 32);
+}
+
 template <typename ST>
 __global__ void __launch_bounds__(256) gemv_simple_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];

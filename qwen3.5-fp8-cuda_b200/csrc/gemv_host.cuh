@@ -55,6 +55,45 @@ static cudaError_t launch_mma_inst(const GemvArgs& a, int grid, int smem, cudaSt
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+// Direct-load kernel (gemv.cuh) for K = 512 J, J in {4, 5, 6, 8, 18}.
+template <typename ST, int J>
+static cudaError_t launch_direct_j(const GemvArgs& a, int rows, cudaStream_t st, bool pdl) {
+  auto kern = gemv_direct_kernel<ST, J>;
+  const int smem = 4 * 512 * J + 8 * 64;
+  static bool attr_done[64] = {};
+  const int d = current_device();
+  if (!attr_done[d]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_done[d] = true;
+  }
+  int grid = (rows + 7) / 8;
+  const int cap = sm_count() * 8;
+  grid = grid < cap ? grid : cap;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid < 1 ? 1 : grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+template <typename ST>
+static cudaError_t launch_direct(const GemvArgs& a, int rows, cudaStream_t st, bool pdl) {
+  switch (a.K) {
+    case 2048: return launch_direct_j<ST, 4>(a, rows, st, pdl);
+    case 2560: return launch_direct_j<ST, 5>(a, rows, st, pdl);
+    case 3072: return launch_direct_j<ST, 6>(a, rows, st, pdl);
+    case 4096: return launch_direct_j<ST, 8>(a, rows, st, pdl);
+    case 9216: return launch_direct_j<ST, 18>(a, rows, st, pdl);
+    default: return cudaErrorNotSupported;
+  }
+}
+
 template <typename ST>
 static cudaError_t launch_simple(const GemvArgs& a, cudaStream_t st, bool pdl) {
   auto kern = gemv_simple_kernel<ST>;
@@ -91,13 +130,17 @@ static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t
 
 // GEMV path selection: 0 = tcgen05 with the weights as the N = 256 operand
 // (default, gemv_tcw.cuh), 1 = mma.sync streaming kernel, 2 = tcgen05 with
-// the weights as the M = 128 operand (gemv_tc.cuh).  QWEN_GEMV_PATH=mma or
-// =tc128 in the environment selects the others (for comparison).
+// the weights as the M = 128 operand (gemv_tc.cuh), 3 = the one-warp-per-row
+// SIMT kernel.  QWEN_GEMV_PATH=mma, =tc128 or =simple in the environment
+// selects the others (for comparison).
 static inline int gemv_path() {
   static int path = -1;
   if (path < 0) {
     const char* e = getenv("QWEN_GEMV_PATH");
-    path = (e && std::strcmp(e, "mma") == 0) ? 1 : (e && std::strcmp(e, "tc128") == 0) ? 2 : 0;
+    path = (e && std::strcmp(e, "mma") == 0)     ? 1
+           : (e && std::strcmp(e, "tc128") == 0)  ? 2
+           : (e && std::strcmp(e, "simple") == 0) ? 3
+                                                  : 0;
   }
   return path;
 }
@@ -109,6 +152,17 @@ static inline long long tcw_min_bytes() {
   if (v < 0) {
     const char* e = getenv("QWEN_TCW_MIN_MB");
     v = (e ? atoll(e) : 48ll) << 20;
+  }
+  return v;
+}
+
+// Weight bytes up to which a plain launch takes the direct-load kernel
+// (QWEN_DIRECT_MAX_MB overrides; default 12 MB).
+static inline long long direct_max_bytes() {
+  static long long v = -1;
+  if (v < 0) {
+    const char* e = getenv("QWEN_DIRECT_MAX_MB");
+    v = (e ? atoll(e) : 12ll) << 20;
   }
   return v;
 }
@@ -378,6 +432,7 @@ static cudaError_t gemv_tcw_run(GemvArgs a, bool f32_scales, cudaStream_t st, bo
 // Validate, plan and launch.  `f32_scales` selects FP32 scale storage.
 // Returns cudaErrorInvalidValue on bad arguments (nothing launched).
 static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool pdl, bool force_simple = false) {
+  if (gemv_path() == 3) force_simple = true;
   if (a.K <= 0 || a.K % 8 != 0 || a.nseg <= 0 || a.nseg > GEMV_MAX_SEG || !a.x) return cudaErrorInvalidValue;
   // Tensor-core path: K a multiple of 128, 16-byte aligned weights, and
   // either every segment a gate/up pair or none.
@@ -400,6 +455,22 @@ static cudaError_t gemv_run(GemvArgs a, bool f32_scales, cudaStream_t st, bool p
     rows += sg.n;
   }
   if (rows == 0) return cudaSuccess;
+  // Plain x, BF16 stores (the reference ABI's launch_gemv_v4_extern and its
+  // grouped forms): the direct-load kernel has the lowest fixed cost (every
+  // weight load of a row issued at once, no ring, no K-split round trips).
+  // The engines' fused launches keep their kernels (and their summation
+  // order); QWEN_GEMV_PATH selects the others.
+  // Up to QWEN_DIRECT_MAX_MB (default 12 MB of weights): above that the
+  // tcgen05 kernels' deeper pipelines win (measured per config-1 shape).
+  if (!force_simple && gemv_path() == 0 && a.pro == PRO_NONE && npair == 0 && aligned16(a.x) &&
+      (long long)rows * a.K <= direct_max_bytes()) {
+    bool direct = true;
+    for (int s = 0; s < a.nseg; ++s) direct &= aligned16(a.seg[s].w) && a.seg[s].epi == EPI_STORE;
+    if (direct) {
+      const cudaError_t e = f32_scales ? launch_direct<float>(a, rows, st, pdl) : launch_direct<bf16>(a, rows, st, pdl);
+      if (e != cudaErrorNotSupported) return e;
+    }
+  }
   if (!force_simple && (gemv_path() == 0 || gemv_path() == 2)) {
     // The N = 256 kernel needs a whole SM per CTA, so it cannot start beside
     // the previous launch; it pays off for gate/up pairs and for launches

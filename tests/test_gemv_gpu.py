@@ -193,11 +193,9 @@ def test_fp8_linear_dispatch():
     assert_close(y.cpu(), ref, what="gemm batch")
     y1 = qops.fp8_linear(x[:1].cuda(), w.cuda(), s.cuda())
     torch.cuda.synchronize()
-    if "QWEN_TCW_MIN_MB" in os.environ or "QWEN_GEMV_PATH" in os.environ:
-        # a forced GEMV kernel may split K differently from the GEMM
-        assert_close(y1.cpu()[0], ref[0], what="gemv row 0")
-    else:
-        assert torch.equal(y1.cpu()[0], y.cpu()[0])
+    # the GEMV (direct-load kernel by default) sums in another order than the GEMM
+    assert_close(y1.cpu()[0], ref[0], what="gemv row 0")
+    assert_rounded(y1.cpu()[0], ref[0], what="gemv row 0")
 
 
 def test_invalid_arguments_launch_nothing(lib):
