@@ -399,6 +399,61 @@ def ref_gpu_gemv_shapes(peak):
     return time_shapes(peak, ref_lib=ref, chained=False)
 
 
+def ref_gpu_engine(steps=30, warmup=3):
+    """The reference's default decode step re-driven on this GPU through its
+    own kernels (oracle.ref_engine: main.py:1509-1604 with fused_kernels.cu
+    built unmodified for sm_100a), at the 4B shapes from position 128; and its
+    delta-rule kernel alone (launch_delta_rule_decode, 32 heads).  None when
+    the build or a GPU is absent."""
+    path = os.path.join(REPO, "oracle", "_ref", "libref_fused.so")
+    if not (os.path.exists(path) and torch.cuda.is_available()):
+        return None
+    import ctypes
+    from oracle.ref_engine import ReferenceKernelEngine
+    from qwen35_b200.config import qwen35_4b
+    from qwen35_b200.weights import random_weights
+    cfg = qwen35_4b()
+    w = random_weights(cfg, seed=0, device="cuda")
+    eng = ReferenceKernelEngine(cfg, w, max_seq=PROMPT_LEN + steps + warmup + 8)
+    eng.pos = PROMPT_LEN
+    tok = 7
+    for _ in range(warmup):
+        _, tok = eng.step(tok)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        _, tok = eng.step(tok)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    out = {"what": "reference decode step (its kernels from oracle/_ref, its torch ops restated), 4B shapes, "
+                   f"positions {PROMPT_LEN}-{PROMPT_LEN + steps}", "ms_per_step": round(ms, 3),
+           "tok_per_s": round(1000.0 / ms, 2)}
+    H, D = cfg.linear_num_value_heads, cfg.linear_value_head_dim
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q, k = (torch.randn(H, D, generator=g, device="cuda").to(torch.bfloat16) for _ in range(2))
+    v = torch.randn(H, D, generator=g, device="cuda").to(torch.bfloat16)
+    gg = -torch.rand(H, generator=g, device="cuda")
+    beta = torch.rand(H, generator=g, device="cuda").to(torch.bfloat16)
+    state = torch.randn(H, D, D, generator=g, device="cuda") * 0.1
+    o = torch.empty(H, D, dtype=torch.bfloat16, device="cuda")
+    P = ctypes.c_void_p
+    args = [P(t.data_ptr()) for t in (q, k, v, gg, beta, state, o)]
+    for _ in range(5):
+        eng.lib.launch_delta_rule_decode(*args, H, D, P(0))
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(100):
+        eng.lib.launch_delta_rule_decode(*args, H, D, P(0))
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 10.0
+    out["delta_rule_decode"] = {"us_per_launch": round(us, 2), "heads": H,
+                                "gbs_state": round(2 * H * D * D * 4 / us / 1e3, 1)}
+    return out
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -432,6 +487,12 @@ def run_reference(args):
                 "rows": rows}
     except Exception as exc:  # context only, never allowed to drop the line
         line["ref_gpu_gemv_shapes"] = {"error": repr(exc)[:200]}
+    try:
+        r = ref_gpu_engine()
+        if r is not None:
+            line["ref_gpu_engine"] = r
+    except Exception as exc:  # context only, never allowed to drop the line
+        line["ref_gpu_engine"] = {"error": repr(exc)[:200]}
     print(json.dumps(line), flush=True)
 
 
@@ -440,7 +501,9 @@ def config_block(args):
                         "decode (E4M3 128x128 block-scaled linear weights incl. LM head)",
             "model": "Qwen3.5-4B (random init)", "global_batch": 1, "prompt_len": PROMPT_LEN,
             "decode_steps": args.steps, "parallelism": f"tp{args.gpus}" if args.gpus > 1 else "single",
-            **({"tp_exchange": "NVLink peer stores of FP32 partials + flags (CUDA IPC), no library collective"}
+            **({"tp_exchange": "step kernel: every stage sharded over the ranks, each CTA stores its outputs on "
+                               "every rank and arrives on every rank's stage counter over NVLink (CUDA IPC peer "
+                               "memory, no library collective)"}
                if args.gpus > 1 else {}),
             "l2": "no flush: each step streams ~4.3 GB of weights (> 126 MB L2)"}
 
@@ -481,9 +544,14 @@ def run_ours(args):
     cfg = qwen35_4b()
     w = random_weights(cfg, seed=args.seed, device="cuda")
     max_seq = PROMPT_LEN + args.warmup + 2 * args.steps + 16
-    if world > 1:
-        # tensor parallel: one decode stream over all ranks (every rank holds
-        # the same full random weights and keeps its shard)
+    if world > 1 and args.engine == "step":
+        # tensor parallel on the step kernel: one decode stream over all ranks,
+        # every stage sharded, outputs stored on every rank over NVLink
+        from qwen35_b200.step_tp import Qwen35StepTPEngine
+        eng = Qwen35StepTPEngine(cfg, w, rank, world, max_seq=max_seq)
+    elif world > 1:
+        # tensor parallel on the per-launch engine (every rank holds the same
+        # full random weights and keeps its shard)
         eng = Qwen35TPDecodeEngine(cfg, w, rank, world, max_seq=max_seq)
         del w
         torch.cuda.empty_cache()
@@ -586,12 +654,17 @@ def run_ours(args):
             head_stage = {"error": repr(exc)[:200]}
     if step_engine:
         # the dominant (only) kernel of a step: the persistent step kernel; one
-        # launch per step, so its launch time is the device time per step
-        roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(step_gbs / peak, 4), "traffic": load_traffic("step_kernel_config3_ncu.txt"),
+        # launch per step, so its launch time is the device time per step.
+        # Tensor parallel: each rank's launch streams its 1/world share.
+        rank_bytes = sbytes // world
+        rank_gbs = rank_bytes / step_s / 1e9
+        traffic = load_traffic("step_kernel_config3_ncu.txt")
+        roofline = {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(rank_gbs / peak, 4), "traffic": traffic if world == 1 else None,
                     "kernel": "step_kernel (persistent, one cooperative launch per token: every GEMV, GatedDeltaNet, "
-                              "attention and LM-head stage)",
-                    "bytes_per_launch": sbytes, "us_per_launch": round(step_s * 1e6, 2), "peak_kind": peak_kind}
+                              "attention and LM-head stage" + (f"; one per GPU, 1/{world} of every stage)"
+                                                               if world > 1 else ")"),
+                    "bytes_per_launch": rank_bytes, "us_per_launch": round(step_s * 1e6, 2), "peak_kind": peak_kind}
     else:
         roofline = {"bound": "hbm", **{k: v for k, v in head_kernel.items() if k != "kernel"}, "peak": peak,
                     "peak_kind": peak_kind, "kernel": head_kernel["kernel"]}

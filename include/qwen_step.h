@@ -132,6 +132,12 @@ typedef struct qwen_step_stage {
   /* GEMV with BF16 weights (packed by qwen_step_pack_bf16; one STORE / ARGMAX /
      SLICES segment, K a multiple of 256): x is used as BF16, no block scales */
   int wbf16;
+  /* Tensor parallel: this rank's share of the stage - GEMV 32-row tiles
+     [shard0, shard0 + shard_n) of the segments' tiles in order, GatedDeltaNet
+     value heads, or attention KV heads (with all their splits); shard_n = 0:
+     the whole stage.  Outputs are written to every rank (qwen_step_create_tp). */
+  int shard0;
+  int shard_n;
 } qwen_step_stage;
 
 /* Bytes of a packed [N, K] matrix: ceil(N/32) * (K/512) * 16400 (0 if K % 512). */
@@ -151,6 +157,21 @@ int qwen_step_pack_bf16(const void* w, int N, int K, void* out, cudaStream_t str
 /* Builds a program from `nstages` stage descriptions (copied; the pointers
  * they hold must stay valid while the program is used) on the current device. */
 int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_out);
+
+/* Tensor-parallel program over `world` GPUs (one process and one program per
+ * GPU, every rank launching once per token).  Every stage output, K-slice
+ * buffer, argmax workspace, token, key, position and the counters
+ * (qwen_step_counter_bytes(nstages), zeroed) must lie in an arena that every
+ * rank allocates with the same layout (qwen_ipc_alloc) and maps from its
+ * peers (qwen_p2p_open): peer_bases[r] = rank r's arena as mapped here
+ * (peer_bases[rank] = local_base).  Each CTA stores its outputs on every rank
+ * and arrives on every rank's stage counter (system scope); waits read
+ * local memory only.  Stages carry this rank's shard (shard0 / shard_n). */
+int qwen_step_create_tp(const qwen_step_stage* stages, int nstages, int world, int rank, void* const* peer_bases,
+                        const void* local_base, void* counters, void** program_out);
+size_t qwen_step_counter_bytes(int nstages);
+/* A zeroed device allocation of `bytes` and its 64-byte CUDA IPC handle. */
+int qwen_ipc_alloc(size_t bytes, void** base_out, void* ipc_handle_out);
 
 /* One launch of the whole program on `stream`. */
 int qwen_step_launch(void* program, cudaStream_t stream);

@@ -107,9 +107,19 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
 // the caller (else *a.pos_ptr).  U: positions per warp in flight; QREG:
 // the scaled queries held in registers (else re-read from shared memory per
 // position, for callers with a tighter register budget).
+// `peer_off` / `world` (tensor-parallel step kernel): the output is also
+// stored at out + peer_off[r] bytes for every rank r < world.
 template <int D, int G, int U = 4, bool QREG = true>
 __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, float* asmem, int* s_last_p,
-                                          unsigned* tl = nullptr, int pos_known = -1) {
+                                          unsigned* tl = nullptr, int pos_known = -1,
+                                          const long long* peer_off = nullptr, int world = 1) {
+  auto put_out = [&](size_t idx, bf16 ob) {
+    if (!peer_off || world == 1) {
+      a.out[idx] = ob;
+      return;
+    }
+    for (int r = 0; r < world; ++r) *reinterpret_cast<bf16*>(reinterpret_cast<char*>(a.out + idx) + peer_off[r]) = ob;
+  };
   constexpr int EPL = D / 32;
   constexpr int NT = ATTN_WARPS * 32;
   float* qsm = asmem;                       // [G][D] scaled query
@@ -280,7 +290,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
         const float gv = bf2f(__ldcg(a.gate + (size_t)h * a.q_stride + d));
         ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv))));
       }
-      a.out[(size_t)h * D + d] = ob;
+      put_out((size_t)h * D + d, ob);
     } else {
       float* part = a.ws_part + ((size_t)h * nsplit + split) * (D + 2);
       if (d == 0) {
@@ -386,7 +396,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
       const int g = idx / D, d = idx % D;
       bf16 ob = f2bf(Os[k] * (1.0f / wl[g]));
       if (a.gate) ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv[k]))));
-      a.out[(size_t)(kh * G + g) * D + d] = ob;
+      put_out((size_t)(kh * G + g) * D + d, ob);
     }
   } else {
     named_bar(1, NT);
@@ -409,7 +419,7 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
         const float gv = bf2f(__ldcg(a.gate + (size_t)h * a.q_stride + d));
         ob = f2bf(bf2f(ob) * bfround(1.0f / (1.0f + expf(-gv))));
       }
-      a.out[(size_t)h * D + d] = ob;
+      put_out((size_t)h * D + d, ob);
     }
   }
   if (threadIdx.x == 0) {

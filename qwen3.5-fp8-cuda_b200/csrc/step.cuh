@@ -131,7 +131,11 @@ struct alignas(16) StStage {
   AttnArgs attn;
   int attn_dim, attn_g;
   int wbf16;           // GEMV: BF16 weights (chunks of 32 rows x 256 K), x kept as BF16
-  int pad_[3];
+  // this rank's share (tensor parallel): GEMV units cover tiles shard0 ..,
+  // GatedDeltaNet heads shard0 .. shard0 + gdn_heads, attention KV heads
+  // shard0 .. shard0 + attn_kv (0 and the whole stage on one GPU)
+  int shard0, attn_kv;
+  int pad_;
 };
 
 // Shared memory plan (bytes from the dynamic shared memory base).
@@ -152,15 +156,47 @@ static_assert(StSmem::xh % 16 == 0 && StSmem::part % 16 == 0 && StSmem::bars % 8
 static_assert(sizeof(StStage) % 16 == 0, "stage descriptors are copied in 16-byte pieces");
 static_assert(StSmem::total <= 227 * 1024, "shared memory");
 
+constexpr int ST_MAX_WORLD = 8;  // ranks of a tensor-parallel program (one GPU each)
+
 struct StProgram {
   const StStage* stages;
   int nstages;
-  unsigned* counters;    // [nstages + 1]: CTAs done with each stage, then with the step
+  // [2 nstages + 1], monotonic over the program's steps (nothing is cleared):
+  // [0, nstages) stage completions, [nstages, 2 nstages) this rank's CTAs done
+  // with each stage (tensor parallel), [2 nstages] this rank's completed
+  // steps x grid, from which a launch takes its epoch e.  One GPU: stage s is
+  // complete when counters[s] (CTAs) reaches (e + 1) x grid.  Tensor
+  // parallel: a rank's CTAs count on its local counter; the last one adds 1
+  // to counters[s] of every rank (release, system scope), and stage s is
+  // complete when the local counters[s] reaches (e + 1) x world.  In the
+  // shared arena.
+  unsigned long long* counters;
   unsigned* abort_flag;  // set by a timed-out wait; every wait then gives up at once
   unsigned* timeline;    // optional [nstages][grid][ST_TL]: %globaltimer (low 32 bits, ns) per stage and CTA
   const int* pos;        // decode position read by the attention stages (constant within a step), or null
   int drop_stage;        // test hook: CTA 0 does not report stage drop_stage done (-1: off)
+  // Tensor parallel (world > 1): rank r's copy of any shared-arena object is
+  // at the local address + peer_off[r] (peer_off[rank] = 0).  Stage outputs,
+  // K slices, counters, the argmax workspace, token, key and position live in
+  // the arena and are written to every rank.
+  int world, rank;
+  long long peer_off[ST_MAX_WORLD];
 };
+
+// rank r's copy of a shared-arena object
+template <typename T>
+__device__ __forceinline__ T* st_peer(const StProgram& P, T* p, int r) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + P.peer_off[r]);
+}
+// a stage output element, stored on every rank
+template <typename T>
+__device__ __forceinline__ void st_put(const StProgram& P, T* p, T v) {
+  if (P.world == 1) {
+    *p = v;
+    return;
+  }
+  for (int r = 0; r < P.world; ++r) *st_peer(P, p, r) = v;
+}
 
 // Timeline fields of one (stage, CTA): the consumers' wait for the previous
 // stage begins / ends, their work ends; the producer issues the stage's first
@@ -217,13 +253,23 @@ __device__ __forceinline__ bool st_mbar_wait(uint32_t bar, uint32_t parity, unsi
 }
 
 // Wait until `count` CTAs have arrived at `counter` (acquire, GPU scope).
-__device__ __forceinline__ bool st_wait_count(const unsigned* counter, unsigned count, unsigned* abort_flag) {
-  if (ld_acquire_gpu_u32(counter) >= count) return true;
+__device__ __forceinline__ unsigned long long st_ld_acq_u64(const unsigned long long* p, bool sys) {
+  unsigned long long v;
+  if (sys)
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until `counter` reaches `count` (acquire; system scope when other GPUs arrive on it).
+__device__ __forceinline__ bool st_wait_count(const unsigned long long* counter, unsigned long long count,
+                                              unsigned* abort_flag, bool sys) {
+  if (st_ld_acq_u64(counter, sys) >= count) return true;
   const uint64_t t0 = globaltimer_ns(), lim = qwen_wait_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 8; ++i)
-      if (ld_acquire_gpu_u32(counter) >= count) return true;
+      if (st_ld_acq_u64(counter, sys) >= count) return true;
     if (st_aborted(abort_flag)) return false;
     if (globaltimer_ns() - t0 > lim) {
       st_abort(abort_flag);
@@ -297,8 +343,9 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
         wb[i] = S.seg[i].w2;
       }
       st_range(S.nunits, u0, u1);
+      const int shard0 = S.shard0;
       for (int u = u0; u < u1 && ok; ++u) {
-        const int t = u / ns, sl = u - t * ns;
+        const int tl = u / ns, sl = u - tl * ns, t = shard0 + tl;
         const uint8_t* a = wa[0];
         const uint8_t* b = wb[0];
         int tb = t0[0];
@@ -325,7 +372,7 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
       st_range(S.gdn_heads, u0, u1);
       const uint8_t* state = reinterpret_cast<const uint8_t*>(S.gdn.state);
       for (int h = u0; h < u1 && ok; ++h) {
-        const uint8_t* src = state + (size_t)h * ST_GDN_D * ST_GDN_D * 4;
+        const uint8_t* src = state + (size_t)(S.shard0 + h) * ST_GDN_D * ST_GDN_D * 4;
         for (int i = 0; i < ST_GDN_SLOTS; ++i) {
           uint32_t slot;
           if (!(ok = acquire(slot))) break;
@@ -335,7 +382,7 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
         }
       }
     } else {  // ST_ATTN: scratch slots, no copy (a plain arrival completes the phase)
-      st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
+      st_range(S.attn_kv * S.attn.nsplit, u0, u1);
       for (int u = u0; u < u1 && ok; ++u) {
         const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
         for (int i = 0; i < cnt; ++i) {
@@ -614,9 +661,60 @@ __device__ __forceinline__ void st_chunk_bf16(const uint8_t* base, const bf16* x
   a1 = (d[0][2] + d[1][2]) + (d[2][2] + d[3][2]);
 }
 
+// Row epilogue of a GEMV stage: gemv_epilogue's arithmetic (gemv.cuh) with
+// every stage output stored on every rank (st_put); the conv state of a row
+// stays with the rank that computes the row.
+__device__ __forceinline__ unsigned long long st_epilogue(const StProgram& P, const GemvSeg& sg, int r, float v,
+                                                          float v2, unsigned long long am_best) {
+  switch (sg.epi) {
+    case EPI_STORE:
+      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(v));
+      break;
+    case EPI_SILU_PAIR:
+      if (sg.y2) reinterpret_cast<bf16*>(sg.y2)[r] = f2bf(v);
+      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(silu_f(v) * v2));
+      break;
+    case EPI_ARGMAX: {
+      const bf16 l = f2bf(v);
+      if (sg.y) st_put(P, reinterpret_cast<bf16*>(sg.y) + r, l);
+      const unsigned long long k = argmax_key(l, (uint32_t)(sg.row_offset + r));
+      am_best = k > am_best ? k : am_best;
+    } break;
+    case EPI_CONV: {
+      const bf16 xb = f2bf(v);
+      if (sg.y2) reinterpret_cast<bf16*>(sg.y2)[r] = xb;
+      const int cw = sg.cw;
+      const bf16* wr = reinterpret_cast<const bf16*>(sg.aux0) + (size_t)r * cw;
+      bf16* st = reinterpret_cast<bf16*>(sg.aux2) + (size_t)r * cw;
+      bf16 win[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) win[t] = t < cw - 1 ? st[t + 1] : xb;
+      float acc = 0.f;
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+        if (t < cw) acc = fmaf(bf2f(wr[t]), bf2f(win[t]), acc);
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+        if (t < cw) st[t] = win[t];
+      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(silu_f(bfround(acc))));
+    } break;
+    case EPI_GATE_G: {
+      const float a = bfround(v) + reinterpret_cast<const float*>(sg.aux1)[r];
+      const float sp = a > 20.0f ? a : log1pf(expf(a));
+      st_put(P, reinterpret_cast<float*>(sg.y) + r, -expf(reinterpret_cast<const float*>(sg.aux0)[r]) * sp);
+    } break;
+    case EPI_GATE_BETA:
+      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(1.0f / (1.0f + expf(-bfround(v)))));
+      break;
+    default:
+      break;
+  }
+  return am_best;
+}
+
 // CTA-wide max of the running argmax keys, the cross-CTA maximum and its
 // finalisation by the last CTA (token, packed key, position increment).
-__device__ __forceinline__ void st_argmax_finish(const StStage& S, unsigned long long best,
+__device__ __forceinline__ void st_argmax_finish(const StProgram& P, const StStage& S, unsigned long long best,
                                                  unsigned long long* misc) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 #pragma unroll
@@ -629,20 +727,32 @@ __device__ __forceinline__ void st_argmax_finish(const StStage& S, unsigned long
   if (tid == 0) {
     best = 0;
     for (int i = 0; i < ST_CW; ++i) best = misc[i] > best ? misc[i] : best;
-    unsigned long long* ws = S.am_ws;
-    if (best) atomicMax(ws, best);
-    __threadfence();
-    unsigned* cnt = reinterpret_cast<unsigned*>(ws + 1);
-    const unsigned prev = atomicAdd(cnt, 1u);
-    if (prev == gridDim.x - 1) {
-      __threadfence();
-      const unsigned long long key = atomicAdd(ws, 0ull);
-      if (S.am_key_out) *S.am_key_out = key;
-      if (S.am_token_out) *S.am_token_out = (long long)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
-      if (S.pos_inc) *S.pos_inc += 1;
-      *ws = 0ull;
-      *cnt = 0u;
-      __threadfence();
+    // every CTA of every rank folds its key into every rank's workspace; the
+    // last arrival on a rank's count finalises that rank (token, key,
+    // position) and clears its workspace
+    const unsigned total = (unsigned)P.world * gridDim.x;
+    for (int r = 0; r < P.world; ++r) {
+      unsigned long long* ws = st_peer(P, S.am_ws, r);
+      if (P.world == 1) {
+        if (best) atomicMax(ws, best);
+        __threadfence();
+      } else {
+        if (best) atomicMax_system(ws, best);
+        __threadfence_system();
+      }
+      unsigned* cnt = reinterpret_cast<unsigned*>(ws + 1);
+      const unsigned prev = P.world == 1 ? atomicAdd(cnt, 1u) : atomicAdd_system(cnt, 1u);
+      if (prev == total - 1) {
+        P.world == 1 ? __threadfence() : __threadfence_system();
+        const unsigned long long key = P.world == 1 ? atomicAdd(ws, 0ull) : atomicAdd_system(ws, 0ull);
+        if (S.am_key_out) *st_peer(P, S.am_key_out, r) = key;
+        if (S.am_token_out)
+          *st_peer(P, S.am_token_out, r) = (long long)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+        if (S.pos_inc) *st_peer(P, S.pos_inc, r) += 1;
+        *ws = 0ull;
+        *cnt = 0u;
+        P.world == 1 ? __threadfence() : __threadfence_system();
+      }
     }
   }
 }
@@ -660,6 +770,7 @@ struct StCtx {
   unsigned* abort_flag;
   unsigned* timeline;  // optional (see StProgram)
   int stage;           // index of the stage being run (timeline)
+  const StProgram* prog;  // the kernel's parameter block (peers, world)
 };
 
 __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32_t& n) {
@@ -726,15 +837,15 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
       } else {
         for (int i = 0; i < ipu; ++i) v += pp[i * ST_ROWS];
       }
-      const int t = u / nslice, sl = u - t * nslice;
+      const int tl = u / nslice, sl = u - tl * nslice, t = S.shard0 + tl;
       const int sg = st_find_seg(S, t);
       const GemvSeg& G = S.seg[sg];
       const int row = (t - S.seg_tile0[sg]) * ST_ROWS + r;
       if (row >= G.n) continue;
       if (S.sl_out) {
-        S.sl_out[(size_t)sl * S.sl_rows + row] = v;
+        st_put(*X.prog, S.sl_out + (size_t)sl * S.sl_rows + row, v);
       } else {
-        am_best = gemv_epilogue(G, row, v, v2, am_best);
+        am_best = st_epilogue(*X.prog, G, row, v, v2, am_best);
       }
     }
     named_bar(1, ST_NT);
@@ -744,7 +855,7 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
     st_tl_put(X.timeline, X.stage, ST_TL_CBLOCK, (unsigned)blocked);
     st_tl_put(X.timeline, X.stage, ST_TL_WCOMP, (unsigned)comp);
   }
-  if (S.am_ws) st_argmax_finish(S, am_best, X.misc);
+  if (S.am_ws) st_argmax_finish(*X.prog, S, am_best, X.misc);
 }
 
 // GatedDeltaNet step of one value head on the consumer warps: thread
@@ -764,7 +875,8 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
   float* ks = X.part + D;
   float* red2 = X.part + 2 * D;  // [2][D]
   float* wsum = X.part + 4 * D;
-  for (int h = u0; h < u1; ++h) {
+  for (int hu = u0; hu < u1; ++hu) {
+    const int h = S.shard0 + hu;  // this rank's heads
     if (tid == 0) {
       int ok = 1;
       for (int i = 0; i < ST_GDN_SLOTS && ok; ++i) {
@@ -846,7 +958,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
         const bf16 core = f2bf(red2[d] + red2[D + d]);
         bf16* out = a.out + (size_t)h * D + d;
         if (!a.gated) {
-          *out = core;
+          st_put(*X.prog, out, core);
         } else {
           const float c = bf2f(core);
           const float cs = warp_sum(c * c);
@@ -856,7 +968,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
           const bf16 normed = f2bf(c * rsqrtf(var + a.eps));
           const bf16 tv = f2bf(bf2f(normed) * nwv);
           const bf16 zs = f2bf(zv / (1.0f + expf(-zv)));
-          *out = f2bf(bf2f(tv) * bf2f(zs));
+          st_put(*X.prog, out, f2bf(bf2f(tv) * bf2f(zs)));
         }
       }
     }
@@ -880,7 +992,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
 __device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32_t& n) {
   const int tid = threadIdx.x;
   int u0, u1;
-  st_range(S.attn.n_kv * S.attn.nsplit, u0, u1);
+  st_range(S.attn_kv * S.attn.nsplit, u0, u1);
   for (int u = u0; u < u1; ++u) {
     const int cnt = st_attn_pad(n) + ST_ATTN_SLOTS;
     bool ok = true;
@@ -891,9 +1003,10 @@ __device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32
       }
     if (named_bar_and(1, ST_NT, ok)) {
       float* scratch = reinterpret_cast<float*>(X.ring + ((n + cnt - ST_ATTN_SLOTS) % ST_SLOTS) * ST_CHUNK);
-      const int kh = u / S.attn.nsplit, split = u - kh * S.attn.nsplit;
+      const int ku = u / S.attn.nsplit, split = u - ku * S.attn.nsplit, kh = S.shard0 + ku;
       unsigned* tl = X.timeline ? X.timeline + ((size_t)X.stage * gridDim.x + blockIdx.x) * ST_TL + ST_TL_PRO : nullptr;
-      attn_unit<256, 4, 2, false>(S.attn, kh, split, scratch, X.flag + 1, tl, X.flag[2]);
+      attn_unit<256, 4, 2, false>(S.attn, kh, split, scratch, X.flag + 1, tl, X.flag[2], X.prog->peer_off,
+                                  X.prog->world);
     }
     named_bar(1, ST_NT);
     if (tid == 0)
@@ -951,6 +1064,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   const int tid = threadIdx.x;
   uint32_t n = 0;
   bool alive = true;
+  const bool sys = P.world > 1;  // other GPUs arrive on the counters: system scope
+  X.prog = &P;
+  // this launch's epoch: the steps this rank has completed (counters[nstages],
+  // local, advanced once per CTA at the end of each step); stage s of this
+  // step is complete when counters[s] reaches (epoch + 1) x world x grid
+  unsigned long long target = 0, local_target = 0;
+  if (tid == 0) {
+    const unsigned long long epoch = st_ld_acq_u64(P.counters + 2 * P.nstages, false) / gridDim.x;
+    local_target = (epoch + 1) * gridDim.x;
+    target = sys ? (epoch + 1) * (unsigned long long)P.world : local_target;
+  }
   // Stage descriptors are read from shared memory: the next stage's one is
   // copied in while the current stage runs, so a stage's first loads do not
   // wait for its descriptor to come from L2.
@@ -961,7 +1085,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     cp_async_wait<0>();  // this thread's pieces of stage s's descriptor
     if (s > 0) {
       bool ok = true;
-      if (tid == 0) ok = st_wait_count(P.counters + s - 1, gridDim.x, P.abort_flag);
+      if (tid == 0) ok = st_wait_count(P.counters + s - 1, target, P.abort_flag, sys);
       alive = named_bar_and(1, ST_NT, ok);
       if (!alive) break;
     } else {
@@ -984,21 +1108,30 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     named_bar(1, ST_NT);
     if (tid == 0) {
       st_stamp(P, s, ST_TL_END);
-      __threadfence();
-      if (s != P.drop_stage || blockIdx.x != 0) atomicAdd(P.counters + s, 1u);
+      if (s != P.drop_stage || blockIdx.x != 0) {
+        if (!sys) {
+          __threadfence();
+          atomicAdd(P.counters + s, 1ull);
+        } else {
+          // this CTA's stores on the other ranks are complete before it counts
+          // itself; the rank's last CTA then tells every rank (one remote add
+          // per rank and stage instead of one per CTA)
+          __threadfence_system();
+          const unsigned long long prev = atomicAdd(P.counters + P.nstages + s, 1ull);
+          if (prev + 1 == local_target) {
+            // (the release of each add orders what this rank's CTAs wrote)
+            for (int r = 0; r < P.world; ++r)
+              asm volatile("red.release.sys.global.add.u64 [%0], 1;" :: "l"(st_peer(P, P.counters + s, r))
+                           : "memory");
+          }
+        }
+      }
     }
   }
-  // End of the step: the last CTA clears the counters for the next launch
-  // (no CTA reads them again in this one).  After an abandoned step they stay
-  // as they are; the host clears them (qwen_step_reset).
-  if (tid == 0 && alive && !st_aborted(P.abort_flag)) {
-    __threadfence();
-    const unsigned prev = atomicAdd(P.counters + P.nstages, 1u);
-    if (prev == gridDim.x - 1) {
-      for (int i = 0; i <= P.nstages; ++i) P.counters[i] = 0u;
-      __threadfence();
-    }
-  }
+  // End of the step: the rank's completed-step count advances once per CTA
+  // (counters keep counting: nothing is cleared).  An abandoned step leaves
+  // it behind; the host clears every counter (qwen_step_reset).
+  if (tid == 0 && alive && !st_aborted(P.abort_flag)) atomicAdd(P.counters + 2 * P.nstages, 1ull);
 }
 
 // ---------------------------------------------------------------------------

@@ -9,6 +9,7 @@
 
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <utility>
 #include <vector>
 
@@ -19,7 +20,11 @@ struct StepProgramHost {
   int grid = 0;
   int nstages = 0;
   qwen::StStage* d_stages = nullptr;
-  unsigned* d_counters = nullptr;  // nstages + 1 counters, then the abort flag
+  unsigned long long* d_counters = nullptr;  // nstages stage counters + the completed-step count
+  bool own_counters = true;                  // allocated here (one GPU) or in the caller's shared arena
+  unsigned* d_abort = nullptr;
+  int world = 1, rank = 0;
+  long long peer_off[qwen::ST_MAX_WORLD] = {};
   unsigned* timeline = nullptr;    // optional per-stage timestamps (qwen_step_set_timeline)
   const int* pos = nullptr;        // the attention stages' position (all of them share one)
   int drop_stage = -1;             // test hook (qwen_step_set_drop)
@@ -160,9 +165,13 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     if (slices && (in.nseg != 1 || !in.sl_out || in.sl_rows < in.seg[0].n)) return cudaErrorInvalidValue;
     if (argmax && (!in.am_ws || in.nseg != 1)) return cudaErrorInvalidValue;
     o.tiles = tiles;
+    // this rank's tiles (tensor parallel): [shard0, shard0 + shard_n)
+    const int my_tiles = in.shard_n > 0 ? in.shard_n : tiles;
+    if (in.shard0 < 0 || in.shard_n < 0 || in.shard0 + my_tiles > tiles) return cudaErrorInvalidValue;
+    o.shard0 = in.shard_n > 0 ? in.shard0 : 0;
     int ns = 1;
     if (slices) {
-      ns = in.nslice > 0 ? in.nslice : step_choose_slices(tiles, o.C, grid);
+      ns = in.nslice > 0 ? in.nslice : step_choose_slices(my_tiles, o.C, grid);
       if (o.C % ns || ns > 16) return cudaErrorInvalidValue;
       o.sl_out = in.sl_out;
       o.sl_rows = in.sl_rows;
@@ -170,7 +179,7 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
       return cudaErrorInvalidValue;
     }
     o.nslice = ns;
-    o.nunits = tiles * ns;
+    o.nunits = my_tiles * ns;
     o.ipu = (o.C / ns) * (o.pair ? 2 : 1);
     if (o.ipu > ST_BATCH) return cudaErrorInvalidValue;
     return cudaSuccess;
@@ -194,7 +203,10 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     a.eps = in.g_eps;
     a.rep = in.g_rep;
     a.gated = in.g_z != nullptr;
-    o.gdn_heads = in.g_heads;
+    if (in.shard0 < 0 || in.shard_n < 0 || in.shard0 + (in.shard_n > 0 ? in.shard_n : in.g_heads) > in.g_heads)
+      return cudaErrorInvalidValue;
+    o.gdn_heads = in.shard_n > 0 ? in.shard_n : in.g_heads;
+    o.shard0 = in.shard_n > 0 ? in.shard0 : 0;
     return cudaSuccess;
   }
   if (in.kind == QWEN_STEP_ATTN) {
@@ -235,6 +247,10 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     a.out = static_cast<bf16*>(in.a_out);
     o.attn_dim = in.a_dim;
     o.attn_g = G;
+    if (in.shard0 < 0 || in.shard_n < 0 || in.shard0 + (in.shard_n > 0 ? in.shard_n : in.a_kv) > in.a_kv)
+      return cudaErrorInvalidValue;
+    o.attn_kv = in.shard_n > 0 ? in.shard_n : in.a_kv;
+    o.shard0 = in.shard_n > 0 ? in.shard0 : 0;
     return cudaSuccess;
   }
   return cudaErrorInvalidValue;
@@ -282,8 +298,15 @@ int qwen_step_pack(const void* w, const void* s, int scale_f32, int N, int K, in
   return record(cudaSuccess);
 }
 
-int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_out) {
+// Shared by qwen_step_create (one GPU) and qwen_step_create_tp.  `counters`:
+// null to allocate the 2 nstages + 1 u64 counters here, else the caller's
+// (inside the shared arena, zeroed).
+static int step_create_impl(const qwen_step_stage* stages, int nstages, int world, int rank,
+                            void* const* peer_bases, const void* local_base, unsigned long long* counters,
+                            void** program_out) {
   if (!stages || nstages <= 0 || !program_out) return record(cudaErrorInvalidValue);
+  if (world < 1 || world > qwen::ST_MAX_WORLD || rank < 0 || rank >= world) return record(cudaErrorInvalidValue);
+  if (world > 1 && (!peer_bases || !local_base || !counters)) return record(cudaErrorInvalidValue);
   *program_out = nullptr;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -320,23 +343,70 @@ int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_
   p->pos = pos;
   p->grid = grid;
   p->nstages = nstages;
+  p->world = world;
+  p->rank = rank;
+  for (int r = 0; r < world; ++r)
+    p->peer_off[r] = world > 1 ? (long long)(static_cast<const char*>(peer_bases[r]) -
+                                             static_cast<const char*>(local_base))
+                               : 0ll;
   for (int i = 0; i < nstages; ++i) {
     const qwen_step_stage& st = stages[i];
     if (st.kind == QWEN_STEP_GEMV && st.am_ws) p->scratch.emplace_back(st.am_ws, 2 * sizeof(unsigned long long));
     if (st.kind == QWEN_STEP_ATTN && st.a_cnt) p->scratch.emplace_back(st.a_cnt, sizeof(unsigned) * st.a_kv);
   }
+  const size_t cbytes = sizeof(unsigned long long) * (2 * nstages + 1);
   e = cudaMalloc(&p->d_stages, sizeof(qwen::StStage) * nstages);
-  if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, sizeof(unsigned) * (nstages + 2));
+  if (e == cudaSuccess) e = cudaMalloc(&p->d_abort, sizeof(unsigned));
+  if (e == cudaSuccess && counters) {
+    p->d_counters = counters;
+    p->own_counters = false;
+  } else if (e == cudaSuccess) {
+    e = cudaMalloc(&p->d_counters, cbytes);
+  }
   if (e == cudaSuccess)
     e = cudaMemcpy(p->d_stages, conv.data(), sizeof(qwen::StStage) * nstages, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemset(p->d_counters, 0, sizeof(unsigned) * (nstages + 2));
+  if (e == cudaSuccess) e = cudaMemset(p->d_counters, 0, cbytes);
+  if (e == cudaSuccess) e = cudaMemset(p->d_abort, 0, sizeof(unsigned));
   if (e != cudaSuccess) {
     cudaFree(p->d_stages);
-    cudaFree(p->d_counters);
+    cudaFree(p->d_abort);
+    if (p->own_counters) cudaFree(p->d_counters);
     delete p;
     return record(e);
   }
   *program_out = p;
+  return 0;
+}
+
+int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_out) {
+  return step_create_impl(stages, nstages, 1, 0, nullptr, nullptr, nullptr, program_out);
+}
+
+int qwen_step_create_tp(const qwen_step_stage* stages, int nstages, int world, int rank, void* const* peer_bases,
+                        const void* local_base, void* counters, void** program_out) {
+  return step_create_impl(stages, nstages, world, rank, peer_bases, local_base,
+                          static_cast<unsigned long long*>(counters), program_out);
+}
+
+size_t qwen_step_counter_bytes(int nstages) {
+  return nstages > 0 ? sizeof(unsigned long long) * (size_t)(2 * nstages + 1) : 0;
+}
+
+int qwen_ipc_alloc(size_t bytes, void** base_out, void* ipc_handle_out) {
+  if (bytes == 0 || !base_out || !ipc_handle_out) return record(cudaErrorInvalidValue);
+  void* base = nullptr;
+  cudaError_t e = cudaMalloc(&base, bytes);
+  if (e != cudaSuccess) return record(e);
+  e = cudaMemset(base, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, base);
+  if (e != cudaSuccess) {
+    cudaFree(base);
+    return record(e);
+  }
+  std::memcpy(ipc_handle_out, &h, sizeof(h));
+  *base_out = base;
   return 0;
 }
 
@@ -347,7 +417,10 @@ int qwen_step_launch(void* program, cudaStream_t stream) {
   P.stages = p->d_stages;
   P.nstages = p->nstages;
   P.counters = p->d_counters;
-  P.abort_flag = p->d_counters + p->nstages + 1;
+  P.abort_flag = p->d_abort;
+  P.world = p->world;
+  P.rank = p->rank;
+  for (int r = 0; r < qwen::ST_MAX_WORLD; ++r) P.peer_off[r] = p->peer_off[r];
   P.timeline = p->timeline;
   P.pos = p->pos;
   P.drop_stage = p->drop_stage;
@@ -367,7 +440,8 @@ int qwen_step_launch(void* program, cudaStream_t stream) {
 int qwen_step_reset(void* program, cudaStream_t stream) {
   StepProgramHost* p = static_cast<StepProgramHost*>(program);
   if (!p) return record(cudaErrorInvalidValue);
-  cudaError_t e = cudaMemsetAsync(p->d_counters, 0, sizeof(unsigned) * (p->nstages + 2), stream);
+  cudaError_t e = cudaMemsetAsync(p->d_counters, 0, sizeof(unsigned long long) * (2 * p->nstages + 1), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(p->d_abort, 0, sizeof(unsigned), stream);
   for (size_t i = 0; i < p->scratch.size() && e == cudaSuccess; ++i)
     e = cudaMemsetAsync(p->scratch[i].first, 0, p->scratch[i].second, stream);
   return record(e);
@@ -384,7 +458,8 @@ int qwen_step_destroy(void* program) {
   StepProgramHost* p = static_cast<StepProgramHost*>(program);
   if (!p) return 0;
   cudaFree(p->d_stages);
-  cudaFree(p->d_counters);
+  cudaFree(p->d_abort);
+  if (p->own_counters) cudaFree(p->d_counters);
   delete p;
   return 0;
 }

@@ -91,6 +91,9 @@ NEW_FUSED = {
     "qwen_step_launch": (I, [P, P]),
     "qwen_step_reset": (I, [P, P]),
     "qwen_step_packed_bytes_bf16": (ctypes.c_size_t, [I, I]),
+    "qwen_step_create_tp": (I, [P, I, I, I, P, P, P, P]),
+    "qwen_step_counter_bytes": (ctypes.c_size_t, [I]),
+    "qwen_ipc_alloc": (I, [ctypes.c_size_t, P, P]),
     "qwen_step_pack_bf16": (I, [P, I, I, P, P]),
     "qwen_step_set_drop": (I, [P, I]),
     "qwen_step_destroy": (I, [P]),

@@ -46,7 +46,9 @@ def test_wait_limit_is_validated(lib):
     from qwen35_b200 import _lib
     assert lib.qwen_set_wait_timeout_ns(10) != 0           # below 1 ms
     assert lib.qwen_set_wait_timeout_ns(10 ** 12) != 0     # above the 2 s maximum
+    assert lib.qwen_last_error() != 0                       # recorded; reading it clears it
     _lib.check(lib.qwen_set_wait_timeout_ns(0), "default")
+    assert lib.qwen_last_error() == 0
 
 
 def _region(lib, world, n):
