@@ -501,9 +501,10 @@ def config_block(args):
                         "decode (E4M3 128x128 block-scaled linear weights incl. LM head)",
             "model": "Qwen3.5-4B (random init)", "global_batch": 1, "prompt_len": PROMPT_LEN,
             "decode_steps": args.steps, "parallelism": f"tp{args.gpus}" if args.gpus > 1 else "single",
-            **({"tp_exchange": "step kernel: every stage sharded over the ranks, each CTA stores its outputs on "
-                               "every rank and arrives on every rank's stage counter over NVLink (CUDA IPC peer "
-                               "memory, no library collective)"}
+            **({"tp_exchange": "step kernel, Megatron-style split: column-parallel in_proj / qkv / gate-up / LM "
+                               "head, row-parallel out_proj / o_proj / down whose FP32 K-slice rows every CTA "
+                               "stores on every rank over NVLink (CUDA IPC peer memory, no library collective); "
+                               "two cross-GPU hand-offs per layer"}
                if args.gpus > 1 else {}),
             "l2": "no flush: each step streams ~4.3 GB of weights (> 126 MB L2)"}
 
@@ -662,7 +663,7 @@ def run_ours(args):
         roofline = {"bound": "hbm", "achieved": round(rank_gbs, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(rank_gbs / peak, 4), "traffic": traffic if world == 1 else None,
                     "kernel": "step_kernel (persistent, one cooperative launch per token: every GEMV, GatedDeltaNet, "
-                              "attention and LM-head stage" + (f"; one per GPU, 1/{world} of every stage)"
+                              "attention and LM-head stage" + (f"; one per GPU, ~1/{world} of every stage)"
                                                                if world > 1 else ")"),
                     "bytes_per_launch": rank_bytes, "us_per_launch": round(step_s * 1e6, 2), "peak_kind": peak_kind}
     else:

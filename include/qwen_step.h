@@ -72,7 +72,7 @@ typedef struct qwen_step_stage {
   /* GEMV */
   int K;                 /* input length, a multiple of 512, at most 9216 (3072 unless PRO_PLAIN) */
   int pro;               /* QWEN_STEP_PRO_* */
-  int nseg;              /* 1..4 segments over one shared input */
+  int nseg;              /* 1..6 segments over one shared input */
   int pair;              /* 1: every segment is a gate/up pair (SILU_PAIR) */
   int nslice;            /* EPI_SLICES: K slices (0: chosen by the library) */
   const void* x;         /* PLAIN / NORM: input BF16 [K]; EMBED_NORM: table BF16 [x_rows][K] */
@@ -91,7 +91,7 @@ typedef struct qwen_step_stage {
   unsigned long long* am_key_out;
   long long* am_token_out;
   int* pos_inc;          /* ARGMAX: ++*pos_inc by the finaliser */
-  qwen_step_seg seg[4];
+  qwen_step_seg seg[6];
   /* GatedDeltaNet (head dim 128; value head h reads key head h / g_rep) */
   const void* g_q;       /* BF16 key-head queries [key heads][128] */
   const void* g_k;
@@ -132,12 +132,26 @@ typedef struct qwen_step_stage {
   /* GEMV with BF16 weights (packed by qwen_step_pack_bf16; one STORE / ARGMAX /
      SLICES segment, K a multiple of 256): x is used as BF16, no block scales */
   int wbf16;
-  /* Tensor parallel: this rank's share of the stage - GEMV 32-row tiles
+  /* A share of the stage (tensor parallel): GEMV 32-row tiles
      [shard0, shard0 + shard_n) of the segments' tiles in order, GatedDeltaNet
      value heads, or attention KV heads (with all their splits); shard_n = 0:
-     the whole stage.  Outputs are written to every rank (qwen_step_create_tp). */
+     the whole stage.  A column-parallel GEMV share is usually described by
+     segments over row ranges instead (seg.w at tile r0 / 32 of the packed
+     matrix, y and the per-row epilogue operands at row r0, ARGMAX row_offset
+     += r0).  Outputs stay on the rank, except EPI_ARGMAX logits. */
   int shard0;
   int shard_n;
+  /* Tensor parallel, GEMV: xrank = 1 for a row-parallel EPI_SLICES stage (this
+     rank's K range of every row): its K-slice rows go to slots [rank x nslice,
+     +nslice) of every rank's sl_out as tagged 8-byte words (FP32 bits | tag
+     << 32; sl_out then holds 16 x sl_rows words, in the IPC arena), and the
+     SLICES_NORM stage reading them polls every word for this step's tag of
+     the producing stage before summing the world x nslice slices in order;
+     nslice x world <= 16.  cstride: chunks per tile row of the packed matrices
+     (K/512 of the whole matrix when seg[].w points at a K range inside it;
+     0: K/512). */
+  int xrank;
+  int cstride;
 } qwen_step_stage;
 
 /* Bytes of a packed [N, K] matrix: ceil(N/32) * (K/512) * 16400 (0 if K % 512). */
@@ -159,14 +173,22 @@ int qwen_step_pack_bf16(const void* w, int N, int K, void* out, cudaStream_t str
 int qwen_step_create(const qwen_step_stage* stages, int nstages, void** program_out);
 
 /* Tensor-parallel program over `world` GPUs (one process and one program per
- * GPU, every rank launching once per token).  Every stage output, K-slice
- * buffer, argmax workspace, token, key, position and the counters
+ * GPU, every rank launching once per token; Megatron-style split): stages
+ * carry this rank's share - column-parallel GEMVs a row range, GatedDeltaNet
+ * / attention the heads those rows feed, row-parallel (xrank) GEMVs the
+ * matching K range of every row.  The K-slice buffers of xrank stages, the
+ * EPI_ARGMAX logits and workspace and the counters
  * (qwen_step_counter_bytes(nstages), zeroed) must lie in an arena that every
  * rank allocates with the same layout (qwen_ipc_alloc) and maps from its
  * peers (qwen_p2p_open): peer_bases[r] = rank r's arena as mapped here
- * (peer_bases[rank] = local_base).  Each CTA stores its outputs on every rank
- * and arrives on every rank's stage counter (system scope); waits read
- * local memory only.  Stages carry this rank's shard (shard0 / shard_n). */
+ * (peer_bases[rank] = local_base).  An xrank stage stores its tagged slice
+ * words on every rank; the next stage polls them in local memory instead of
+ * waiting on a counter (one NVLink crossing, no fence).  Other stages
+ * synchronise within their GPU (counters[nstages, 2 nstages]; counters[0,
+ * nstages) are unused).  The argmax keys are folded into every rank's
+ * workspace; each rank finalises its own token.  Every rank must run the same
+ * steps: the tags derive from the count of completed steps (a reset on one
+ * rank needs a reset on all). */
 int qwen_step_create_tp(const qwen_step_stage* stages, int nstages, int world, int rank, void* const* peer_bases,
                         const void* local_base, void* counters, void** program_out);
 size_t qwen_step_counter_bytes(int nstages);

@@ -87,7 +87,7 @@ constexpr int ST_NORM_MAXK = 3072;             // longest input of a normalising
 constexpr int ST_NORM_MAXB = ST_NORM_MAXK / 128 / ST_CW;
 constexpr int ST_SL_REG = 4;                   // K-slice rows a prologue loads in one round trip
 constexpr int ST_BATCH = 48;                   // chunk partials held before a reduction
-constexpr int ST_MAX_SEG = 4;
+constexpr int ST_MAX_SEG = 6;
 constexpr int ST_ATTN_SLOTS = QWEN_STEP_ATTN_SLOTS;  // contiguous ring slots of scratch for an attention unit
 constexpr int ST_GDN_D = 128;                  // GatedDeltaNet head dim of the step kernel
 constexpr int ST_GDN_SLOTS = ST_GDN_D * ST_GDN_D * 4 / ST_WBYTES;  // 4: one head's FP32 state
@@ -135,6 +135,13 @@ struct alignas(16) StStage {
   // GatedDeltaNet heads shard0 .. shard0 + gdn_heads, attention KV heads
   // shard0 .. shard0 + attn_kv (0 and the whole stage on one GPU)
   int shard0, attn_kv;
+  // tensor parallel: the stage's K-slice partial rows go to every rank as
+  // tagged words (row-parallel projections); other stages stay on their rank
+  int xrank;
+  int cstride;         // GEMV: chunks per tile row of the packed matrices (> C when a rank takes a K range)
+  // SLICES_NORM prologue: index of the xrank stage whose tagged slices it
+  // sums (polled until they carry that stage's tag of this step), or -1
+  int sl_src;
   int pad_;
 };
 
@@ -188,6 +195,10 @@ template <typename T>
 __device__ __forceinline__ T* st_peer(const StProgram& P, T* p, int r) {
   return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + P.peer_off[r]);
 }
+template <typename T>
+__device__ __forceinline__ void st_put_local(T* p, T v) {
+  *p = v;
+}
 // a stage output element, stored on every rank
 template <typename T>
 __device__ __forceinline__ void st_put(const StProgram& P, T* p, T v) {
@@ -196,6 +207,24 @@ __device__ __forceinline__ void st_put(const StProgram& P, T* p, T v) {
     return;
   }
   for (int r = 0; r < P.world; ++r) *st_peer(P, p, r) = v;
+}
+
+// Tagged K-slice words of a row-parallel stage (tensor parallel): the FP32
+// value's bits | tag << 32, stored on every rank with one 8-byte store each.
+// 64-bit accesses are single-copy atomic, so a reader that sees the tag of
+// this step's stage sees the value; no fence or counter orders them.
+__device__ __forceinline__ void st_put_tagged(const StProgram& P, unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  for (int r = 0; r < P.world; ++r)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(st_peer(P, p, r)), "l"(w) : "memory");
+}
+__device__ __forceinline__ void st_ll_load(const unsigned long long* p, ulonglong2& a, ulonglong2& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a.x), "=l"(a.y) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(b.x), "=l"(b.y) : "l"(p + 2) : "memory");
+}
+__device__ __forceinline__ bool st_ll_ok(const ulonglong2& a, const ulonglong2& b, uint32_t tag) {
+  return ((uint32_t)(a.x >> 32) == tag) & ((uint32_t)(a.y >> 32) == tag) & ((uint32_t)(b.x >> 32) == tag) &
+         ((uint32_t)(b.y >> 32) == tag);
 }
 
 // Timeline fields of one (stage, CTA): the consumers' wait for the previous
@@ -332,7 +361,7 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
       // the stage's fields in registers: the copies below are asm with memory
       // clobbers, after which the compiler would reload them from global memory
       const int ns = S.nslice, ipu = S.ipu, pair = S.pair, nseg = S.nseg;
-      const size_t tile_bytes = (size_t)S.C * ST_CHUNK, slice_bytes = (size_t)(S.C / ns) * ST_CHUNK;
+      const size_t tile_bytes = (size_t)S.cstride * ST_CHUNK, slice_bytes = (size_t)(S.C / ns) * ST_CHUNK;
       int t0[ST_MAX_SEG];
       const uint8_t* wa[ST_MAX_SEG];
       const uint8_t* wb[ST_MAX_SEG];
@@ -423,10 +452,50 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
 // would cost a round trip each.  MB: 128-blocks per warp this instantiation
 // holds (norm stages: K <= 3072); SLR: K-slice rows loaded with the first
 // round trip (0 for the plain prologue).
+// Four K-slice values at element `idx` of a slice buffer: FP32, or the low
+// halves of tagged words (tensor parallel, already seen with their tag).
+__device__ __forceinline__ float4 st_slice4(const float* sl, size_t idx, bool tagged) {
+  if (!tagged) return __ldcg(reinterpret_cast<const float4*>(sl + idx));
+  ulonglong2 a, b;
+  st_ll_load(reinterpret_cast<const unsigned long long*>(sl) + idx, a, b);
+  return make_float4(__uint_as_float((uint32_t)a.x), __uint_as_float((uint32_t)a.y), __uint_as_float((uint32_t)b.x),
+                     __uint_as_float((uint32_t)b.y));
+}
+
+// Wait until every tagged word this thread's prologue reads (nsl slices of
+// the 128-blocks warp, warp + 8, ... of K) carries `tag`: all tags loaded at
+// once, the whole set again while any is missing (bounded by the wait limit
+// and the abort flag; on time-out the step is abandoned with error 8).
+__device__ __noinline__ void st_ll_wait_all(const unsigned long long* sl, int nsl, int stride, int nb, uint32_t tag,
+                                            unsigned* abort_flag) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint64_t t0 = 0;
+  for (int tries = 0;; ++tries) {
+    bool ok = true;
+    for (int c = 0; c < nsl; ++c)
+#pragma unroll 4
+      for (int b = warp; b < nb; b += ST_CW) {
+        ulonglong2 x, y;
+        st_ll_load(sl + (size_t)c * stride + b * 128 + lane * 4, x, y);
+        ok &= st_ll_ok(x, y, tag);
+      }
+    if (ok || st_aborted(abort_flag)) return;
+    if (tries == 0) t0 = globaltimer_ns();
+    if (globaltimer_ns() - t0 > qwen_wait_ns()) {
+      st_abort(abort_flag);
+      return;
+    }
+  }
+}
+
 template <int MB, int SLR>
-__device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8_t* xl, float* xinv, float* red) {
+__device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8_t* xl, float* xinv, float* red,
+                                            uint32_t ll_tag, unsigned* abort_flag) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = S.K, nb = K >> 7, pro = S.pro, nsl = S.sl_in_count, sl_stride = S.sl_stride;
+  // tagged slices of a row-parallel stage (tensor parallel): waited for
+  // first, then read like FP32 slices (the low halves of the words)
+  const bool ll = pro == STP_SLICES_NORM && S.sl_src >= 0;
   const float* sl_in = S.sl_in;
   const float* norm_w = S.norm_w;
   const bool norm = pro != STP_PLAIN;
@@ -447,6 +516,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   float4 wv[MB];
   float4 sp[MB][SLR > 0 ? SLR : 1];
   const int nreg = pro == STP_SLICES_NORM ? (nsl < SLR ? nsl : SLR) : 0;
+  if (ll) st_ll_wait_all(reinterpret_cast<const unsigned long long*>(sl_in), nsl, sl_stride, nb, ll_tag, abort_flag);
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
     const int b = warp + i * ST_CW;
@@ -457,7 +527,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
       if (norm) wv[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k0));
 #pragma unroll
       for (int c = 0; c < SLR; ++c)
-        if (c < nreg) sp[i][c] = __ldcg(reinterpret_cast<const float4*>(sl_in + (size_t)c * sl_stride + k0));
+        if (c < nreg) sp[i][c] = st_slice4(sl_in, (size_t)c * sl_stride + k0, ll);
     }
   }
   float v[MB][4];
@@ -477,15 +547,24 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
           sum[i][0] += sp[i][c].x; sum[i][1] += sp[i][c].y; sum[i][2] += sp[i][c].z; sum[i][3] += sp[i][c].w;
         }
     }
-    // slices beyond SLR (rare): one more round trip each, in order
-    for (int c = nreg; c < nsl; ++c)
+    // slices beyond SLR: SLR more rows per round trip, added in slice order
+    for (int c0 = nreg; c0 < nsl; c0 += SLR) {
 #pragma unroll
       for (int i = 0; i < MB; ++i) {
         const int b = warp + i * ST_CW;
-        if (b >= nb) continue;
-        const float4 p = __ldcg(reinterpret_cast<const float4*>(sl_in + (size_t)c * sl_stride + b * 128 + lane * 4));
-        sum[i][0] += p.x; sum[i][1] += p.y; sum[i][2] += p.z; sum[i][3] += p.w;
+#pragma unroll
+        for (int c = 0; c < SLR; ++c)
+          if (b < nb && c0 + c < nsl)
+            sp[i][c] = st_slice4(sl_in, (size_t)(c0 + c) * sl_stride + b * 128 + lane * 4, ll);
       }
+#pragma unroll
+      for (int i = 0; i < MB; ++i)
+#pragma unroll
+        for (int c = 0; c < SLR; ++c)
+          if (c0 + c < nsl) {
+            sum[i][0] += sp[i][c].x; sum[i][1] += sp[i][c].y; sum[i][2] += sp[i][c].z; sum[i][3] += sp[i][c].w;
+          }
+    }
 #pragma unroll
     for (int i = 0; i < MB; ++i)
 #pragma unroll
@@ -661,22 +740,21 @@ __device__ __forceinline__ void st_chunk_bf16(const uint8_t* base, const bf16* x
   a1 = (d[0][2] + d[1][2]) + (d[2][2] + d[3][2]);
 }
 
-// Row epilogue of a GEMV stage: gemv_epilogue's arithmetic (gemv.cuh) with
-// every stage output stored on every rank (st_put); the conv state of a row
-// stays with the rank that computes the row.
+// Row epilogue of a GEMV stage: gemv_epilogue's arithmetic (gemv.cuh).
 __device__ __forceinline__ unsigned long long st_epilogue(const StProgram& P, const GemvSeg& sg, int r, float v,
                                                           float v2, unsigned long long am_best) {
+  // (tensor parallel: these stages keep their outputs on their rank)
   switch (sg.epi) {
     case EPI_STORE:
-      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(v));
+      st_put_local(reinterpret_cast<bf16*>(sg.y) + r, f2bf(v));
       break;
     case EPI_SILU_PAIR:
       if (sg.y2) reinterpret_cast<bf16*>(sg.y2)[r] = f2bf(v);
-      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(silu_f(v) * v2));
+      st_put_local(reinterpret_cast<bf16*>(sg.y) + r, f2bf(silu_f(v) * v2));
       break;
     case EPI_ARGMAX: {
       const bf16 l = f2bf(v);
-      if (sg.y) st_put(P, reinterpret_cast<bf16*>(sg.y) + r, l);
+      if (sg.y) st_put(P, reinterpret_cast<bf16*>(sg.y) + r, l);  // logits (optional) on every rank
       const unsigned long long k = argmax_key(l, (uint32_t)(sg.row_offset + r));
       am_best = k > am_best ? k : am_best;
     } break;
@@ -696,15 +774,15 @@ __device__ __forceinline__ unsigned long long st_epilogue(const StProgram& P, co
 #pragma unroll
       for (int t = 0; t < 8; ++t)
         if (t < cw) st[t] = win[t];
-      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(silu_f(bfround(acc))));
+      st_put_local(reinterpret_cast<bf16*>(sg.y) + r, f2bf(silu_f(bfround(acc))));
     } break;
     case EPI_GATE_G: {
       const float a = bfround(v) + reinterpret_cast<const float*>(sg.aux1)[r];
       const float sp = a > 20.0f ? a : log1pf(expf(a));
-      st_put(P, reinterpret_cast<float*>(sg.y) + r, -expf(reinterpret_cast<const float*>(sg.aux0)[r]) * sp);
+      st_put_local(reinterpret_cast<float*>(sg.y) + r, -expf(reinterpret_cast<const float*>(sg.aux0)[r]) * sp);
     } break;
     case EPI_GATE_BETA:
-      st_put(P, reinterpret_cast<bf16*>(sg.y) + r, f2bf(1.0f / (1.0f + expf(-bfround(v)))));
+      st_put_local(reinterpret_cast<bf16*>(sg.y) + r, f2bf(1.0f / (1.0f + expf(-bfround(v)))));
       break;
     default:
       break;
@@ -727,31 +805,45 @@ __device__ __forceinline__ void st_argmax_finish(const StProgram& P, const StSta
   if (tid == 0) {
     best = 0;
     for (int i = 0; i < ST_CW; ++i) best = misc[i] > best ? misc[i] : best;
-    // every CTA of every rank folds its key into every rank's workspace; the
-    // last arrival on a rank's count finalises that rank (token, key,
-    // position) and clears its workspace
+    // every CTA of every rank folds its key into every rank's workspace and
+    // counts itself there; CTA 0 of each rank then waits for all of them
+    // (bounded) and finalises its own rank (token, key, position) and clears
+    // the workspace
     const unsigned total = (unsigned)P.world * gridDim.x;
+    const bool sys = P.world > 1;
+    for (int r = 0; r < P.world; ++r)
+      if (best) sys ? (void)atomicMax_system(st_peer(P, S.am_ws, r), best) : (void)atomicMax(S.am_ws, best);
+    sys ? __threadfence_system() : __threadfence();
     for (int r = 0; r < P.world; ++r) {
-      unsigned long long* ws = st_peer(P, S.am_ws, r);
-      if (P.world == 1) {
-        if (best) atomicMax(ws, best);
-        __threadfence();
-      } else {
-        if (best) atomicMax_system(ws, best);
-        __threadfence_system();
-      }
+      unsigned* cnt = reinterpret_cast<unsigned*>(st_peer(P, S.am_ws, r) + 1);
+      sys ? (void)atomicAdd_system(cnt, 1u) : (void)atomicAdd(cnt, 1u);
+    }
+    if (blockIdx.x == 0) {
+      unsigned long long* ws = S.am_ws;
       unsigned* cnt = reinterpret_cast<unsigned*>(ws + 1);
-      const unsigned prev = P.world == 1 ? atomicAdd(cnt, 1u) : atomicAdd_system(cnt, 1u);
-      if (prev == total - 1) {
-        P.world == 1 ? __threadfence() : __threadfence_system();
-        const unsigned long long key = P.world == 1 ? atomicAdd(ws, 0ull) : atomicAdd_system(ws, 0ull);
-        if (S.am_key_out) *st_peer(P, S.am_key_out, r) = key;
-        if (S.am_token_out)
-          *st_peer(P, S.am_token_out, r) = (long long)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
-        if (S.pos_inc) *st_peer(P, S.pos_inc, r) += 1;
+      const uint64_t t0 = globaltimer_ns(), lim = qwen_wait_ns();
+      bool ok = true;
+      while (true) {
+        unsigned c;
+        if (sys)
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(cnt) : "memory");
+        else
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(cnt) : "memory");
+        if (c >= total) break;
+        if (st_aborted(P.abort_flag) || globaltimer_ns() - t0 > lim) {
+          st_abort(P.abort_flag);
+          ok = false;
+          break;
+        }
+      }
+      if (ok) {
+        const unsigned long long key = *reinterpret_cast<volatile unsigned long long*>(ws);
+        if (S.am_key_out) *S.am_key_out = key;
+        if (S.am_token_out) *S.am_token_out = (long long)(0xffffffffu - (uint32_t)(key & 0xffffffffu));
+        if (S.pos_inc) *S.pos_inc += 1;
         *ws = 0ull;
         *cnt = 0u;
-        P.world == 1 ? __threadfence() : __threadfence_system();
+        __threadfence();
       }
     }
   }
@@ -771,6 +863,7 @@ struct StCtx {
   unsigned* timeline;  // optional (see StProgram)
   int stage;           // index of the stage being run (timeline)
   const StProgram* prog;  // the kernel's parameter block (peers, world)
+  uint32_t tag0;       // tag of stage 0 of this step (tensor parallel): epoch x nstages + 1
 };
 
 __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32_t& n) {
@@ -778,9 +871,9 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
   int u0, u1;
   st_range(S.nunits, u0, u1);
   if (S.pro == STP_PLAIN)
-    st_prologue<ST_MAXB, 0>(S, X.xh, X.xl, X.xinv, X.red);
+    st_prologue<ST_MAXB, 0>(S, X.xh, X.xl, X.xinv, X.red, 0u, X.abort_flag);
   else
-    st_prologue<ST_NORM_MAXB, ST_SL_REG>(S, X.xh, X.xl, X.xinv, X.red);
+    st_prologue<ST_NORM_MAXB, ST_SL_REG>(S, X.xh, X.xl, X.xinv, X.red, X.tag0 + (uint32_t)S.sl_src, X.abort_flag);
   if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_PRO, (unsigned)globaltimer_ns());
   const int ipu = S.ipu, nslice = S.nslice, pair = S.pair;
   const int upb = ST_BATCH / ipu > 0 ? ST_BATCH / ipu : 1;
@@ -843,7 +936,13 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
       const int row = (t - S.seg_tile0[sg]) * ST_ROWS + r;
       if (row >= G.n) continue;
       if (S.sl_out) {
-        st_put(*X.prog, S.sl_out + (size_t)sl * S.sl_rows + row, v);
+        if (S.xrank)  // rank r's slices are slots [r nslice, (r + 1) nslice) on every rank
+          st_put_tagged(*X.prog,
+                        reinterpret_cast<unsigned long long*>(S.sl_out) +
+                            (size_t)(X.prog->rank * nslice + sl) * S.sl_rows + row,
+                        v, X.tag0 + (uint32_t)X.stage);
+        else
+          S.sl_out[(size_t)sl * S.sl_rows + row] = v;
       } else {
         am_best = st_epilogue(*X.prog, G, row, v, v2, am_best);
       }
@@ -958,7 +1057,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
         const bf16 core = f2bf(red2[d] + red2[D + d]);
         bf16* out = a.out + (size_t)h * D + d;
         if (!a.gated) {
-          st_put(*X.prog, out, core);
+          *out = core;
         } else {
           const float c = bf2f(core);
           const float cs = warp_sum(c * c);
@@ -968,7 +1067,7 @@ __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_
           const bf16 normed = f2bf(c * rsqrtf(var + a.eps));
           const bf16 tv = f2bf(bf2f(normed) * nwv);
           const bf16 zs = f2bf(zv / (1.0f + expf(-zv)));
-          st_put(*X.prog, out, f2bf(bf2f(tv) * bf2f(zs)));
+          *out = f2bf(bf2f(tv) * bf2f(zs));
         }
       }
     }
@@ -1005,8 +1104,7 @@ __device__ __forceinline__ void st_attn(const StStage& S, const StCtx& X, uint32
       float* scratch = reinterpret_cast<float*>(X.ring + ((n + cnt - ST_ATTN_SLOTS) % ST_SLOTS) * ST_CHUNK);
       const int ku = u / S.attn.nsplit, split = u - ku * S.attn.nsplit, kh = S.shard0 + ku;
       unsigned* tl = X.timeline ? X.timeline + ((size_t)X.stage * gridDim.x + blockIdx.x) * ST_TL + ST_TL_PRO : nullptr;
-      attn_unit<256, 4, 2, false>(S.attn, kh, split, scratch, X.flag + 1, tl, X.flag[2], X.prog->peer_off,
-                                  X.prog->world);
+      attn_unit<256, 4, 2, false>(S.attn, kh, split, scratch, X.flag + 1, tl, X.flag[2]);
     }
     named_bar(1, ST_NT);
     if (tid == 0)
@@ -1064,16 +1162,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   const int tid = threadIdx.x;
   uint32_t n = 0;
   bool alive = true;
-  const bool sys = P.world > 1;  // other GPUs arrive on the counters: system scope
   X.prog = &P;
-  // this launch's epoch: the steps this rank has completed (counters[nstages],
-  // local, advanced once per CTA at the end of each step); stage s of this
-  // step is complete when counters[s] reaches (epoch + 1) x world x grid
-  unsigned long long target = 0, local_target = 0;
+  // this launch's epoch: the steps this rank has completed (counters[2 nstages],
+  // advanced once per CTA at the end of each step); stage s of this step is
+  // complete when counters[nstages + s] reaches (epoch + 1) x grid.  The tag of
+  // stage s's K-slice words (tensor parallel) is epoch x nstages + 1 + s.
+  unsigned long long local_target = 0;
+  int prev_xrank = 0;  // thread 0: the previous stage's slices are tagged words
   if (tid == 0) {
     const unsigned long long epoch = st_ld_acq_u64(P.counters + 2 * P.nstages, false) / gridDim.x;
     local_target = (epoch + 1) * gridDim.x;
-    target = sys ? (epoch + 1) * (unsigned long long)P.world : local_target;
+    X.flag[3] = (int)(uint32_t)(epoch * (unsigned long long)P.nstages + 1ull);
   }
   // Stage descriptors are read from shared memory: the next stage's one is
   // copied in while the current stage runs, so a stage's first loads do not
@@ -1085,11 +1184,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     cp_async_wait<0>();  // this thread's pieces of stage s's descriptor
     if (s > 0) {
       bool ok = true;
-      if (tid == 0) ok = st_wait_count(P.counters + s - 1, target, P.abort_flag, sys);
+      // after a row-parallel stage nothing is counted: the prologue polls the
+      // tagged slices of every rank (which also orders this stage after the
+      // previous one: a CTA that wrote slices had passed the wait before it)
+      if (tid == 0 && !prev_xrank)
+        ok = st_wait_count(P.counters + P.nstages + s - 1, local_target, P.abort_flag, false);
+      if (tid == 0 && prev_xrank) ok = !st_aborted(P.abort_flag);
       alive = named_bar_and(1, ST_NT, ok);
       if (!alive) break;
     } else {
       named_bar(1, ST_NT);
+      X.tag0 = (uint32_t)X.flag[3];
     }
     const StStage& S = desc[s & 1];
     // the other buffer held stage s - 1, which every consumer has finished
@@ -1109,23 +1214,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     if (tid == 0) {
       st_stamp(P, s, ST_TL_END);
       if (s != P.drop_stage || blockIdx.x != 0) {
-        if (!sys) {
-          __threadfence();
-          atomicAdd(P.counters + s, 1ull);
-        } else {
-          // this CTA's stores on the other ranks are complete before it counts
-          // itself; the rank's last CTA then tells every rank (one remote add
-          // per rank and stage instead of one per CTA)
-          __threadfence_system();
-          const unsigned long long prev = atomicAdd(P.counters + P.nstages + s, 1ull);
-          if (prev + 1 == local_target) {
-            // (the release of each add orders what this rank's CTAs wrote)
-            for (int r = 0; r < P.world; ++r)
-              asm volatile("red.release.sys.global.add.u64 [%0], 1;" :: "l"(st_peer(P, P.counters + s, r))
-                           : "memory");
-          }
-        }
+        __threadfence();
+        atomicAdd(P.counters + P.nstages + s, 1ull);
       }
+      prev_xrank = S.xrank;
     }
   }
   // End of the step: the rank's completed-step count advances once per CTA

@@ -57,10 +57,10 @@ double step_slice_cost() {
 
 // K slices of a single-segment EPI_SLICES stage: a divisor of C that
 // minimises the busiest CTA's chunks plus the slices' read cost.
-int step_choose_slices(int tiles, int C, int grid) {
+int step_choose_slices(int tiles, int C, int grid, int max_slices = 16) {
   int best = 1;
   double best_cost = 1e30;
-  for (int s = 1; s <= C && s <= 16; ++s) {
+  for (int s = 1; s <= C && s <= max_slices; ++s) {
     if (C % s) continue;
     const long long units = (long long)tiles * s;
     const long long per_cta = (units + grid - 1) / grid;
@@ -73,8 +73,8 @@ int step_choose_slices(int tiles, int C, int grid) {
   return best;
 }
 
-cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, const std::vector<qwen::StStage>& prev,
-                         const std::vector<qwen_step_stage>& prev_in) {
+cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, int world,
+                         const std::vector<qwen::StStage>& prev, const std::vector<qwen_step_stage>& prev_in) {
   using namespace qwen;
   o = StStage{};
   o.kind = in.kind;
@@ -105,11 +105,20 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     o.sl_in = in.sl_in;
     o.sl_stride = in.sl_stride;
     o.sl_in_count = in.sl_in_count;
-    if (in.pro == QWEN_STEP_PRO_SLICES_NORM && o.sl_in_count <= 0) {
-      // the slice count of the latest earlier stage writing these rows
-      for (int i = (int)prev.size() - 1; i >= 0 && o.sl_in_count <= 0; --i)
-        if (prev_in[i].sl_out == in.sl_in) o.sl_in_count = prev[i].nslice;
-      if (o.sl_in_count <= 0) return cudaErrorInvalidValue;
+    o.sl_src = -1;
+    if (in.pro == QWEN_STEP_PRO_SLICES_NORM) {
+      // the latest earlier stage writing these rows: its slice count, and
+      // whether they are tagged words from every rank (row-parallel stage)
+      int src = -1;
+      for (int i = (int)prev.size() - 1; i >= 0 && src < 0; --i)
+        if (prev_in[i].sl_out == in.sl_in) src = i;
+      if (src >= 0 && prev[src].xrank) {
+        o.sl_src = src;
+        o.sl_in_count = prev[src].nslice * world;
+      } else if (o.sl_in_count <= 0) {
+        if (src < 0) return cudaErrorInvalidValue;
+        o.sl_in_count = prev[src].nslice;
+      }
     }
     if (o.sl_in_count > 16) return cudaErrorInvalidValue;
     o.am_ws = in.am_ws;
@@ -171,7 +180,9 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     o.shard0 = in.shard_n > 0 ? in.shard0 : 0;
     int ns = 1;
     if (slices) {
-      ns = in.nslice > 0 ? in.nslice : step_choose_slices(my_tiles, o.C, grid);
+      // (a cross-rank stage's W x nslice slices fill the 16 slice rows)
+      const int cap = (world > 1 && in.xrank) ? 16 / world : 16;
+      ns = in.nslice > 0 ? in.nslice : step_choose_slices(my_tiles, o.C, grid, cap);
       if (o.C % ns || ns > 16) return cudaErrorInvalidValue;
       o.sl_out = in.sl_out;
       o.sl_rows = in.sl_rows;
@@ -180,6 +191,12 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     }
     o.nslice = ns;
     o.nunits = my_tiles * ns;
+    // tensor parallel: a row-parallel stage (this rank's K range, every row)
+    // writes its K-slice rows to every rank and is counted across the ranks
+    o.xrank = (world > 1 && in.xrank) ? 1 : 0;
+    if (o.xrank && (!slices || ns * world > 16)) return cudaErrorInvalidValue;
+    o.cstride = in.cstride > 0 ? in.cstride : o.C;
+    if (o.cstride < o.C) return cudaErrorInvalidValue;
     o.ipu = (o.C / ns) * (o.pair ? 2 : 1);
     if (o.ipu > ST_BATCH) return cudaErrorInvalidValue;
     return cudaSuccess;
@@ -327,7 +344,7 @@ static int step_create_impl(const qwen_step_stage* stages, int nstages, int worl
   conv.reserve(nstages);
   for (int i = 0; i < nstages; ++i) {
     qwen::StStage o;
-    e = step_convert(stages[i], o, grid, conv, ins);
+    e = step_convert(stages[i], o, grid, world, conv, ins);
     if (e != cudaSuccess) return record(e);
     conv.push_back(o);
     ins.push_back(stages[i]);
@@ -351,8 +368,15 @@ static int step_create_impl(const qwen_step_stage* stages, int nstages, int worl
                                : 0ll;
   for (int i = 0; i < nstages; ++i) {
     const qwen_step_stage& st = stages[i];
-    if (st.kind == QWEN_STEP_GEMV && st.am_ws) p->scratch.emplace_back(st.am_ws, 2 * sizeof(unsigned long long));
-    if (st.kind == QWEN_STEP_ATTN && st.a_cnt) p->scratch.emplace_back(st.a_cnt, sizeof(unsigned) * st.a_kv);
+    auto add = [&](void* ptr, size_t bytes) {
+      for (auto& e2 : p->scratch)
+        if (e2.first == ptr) return;
+      p->scratch.emplace_back(ptr, bytes);
+    };
+    if (st.kind == QWEN_STEP_GEMV && st.am_ws) add(st.am_ws, 2 * sizeof(unsigned long long));
+    // tagged slice words: a reset program restarts its tags, so old words must not match
+    if (st.kind == QWEN_STEP_GEMV && conv[i].xrank) add(st.sl_out, sizeof(unsigned long long) * 16 * (size_t)st.sl_rows);
+    if (st.kind == QWEN_STEP_ATTN && st.a_cnt) add(st.a_cnt, sizeof(unsigned) * st.a_kv);
   }
   const size_t cbytes = sizeof(unsigned long long) * (2 * nstages + 1);
   e = cudaMalloc(&p->d_stages, sizeof(qwen::StStage) * nstages);

@@ -53,7 +53,7 @@ class StepStage(ctypes.Structure):
         ("token", P), ("sl_in", P), ("sl_in_count", ctypes.c_int), ("sl_stride", ctypes.c_int),
         ("sl_out", P), ("sl_rows", ctypes.c_int),
         ("am_ws", P), ("am_key_out", P), ("am_token_out", P), ("pos_inc", P),
-        ("seg", StepSeg * 4),
+        ("seg", StepSeg * 6),
         ("g_q", P), ("g_k", P), ("g_v", P), ("g_g", P), ("g_beta", P), ("g_state", P), ("g_out", P),
         ("g_z", P), ("g_norm_w", P), ("g_eps", ctypes.c_float), ("g_heads", ctypes.c_int),
         ("g_dim", ctypes.c_int), ("g_rep", ctypes.c_int),
@@ -62,7 +62,8 @@ class StepStage(ctypes.Structure):
         ("a_heads", ctypes.c_int), ("a_kv", ctypes.c_int), ("a_dim", ctypes.c_int), ("a_rot", ctypes.c_int),
         ("a_eps", ctypes.c_float), ("a_chunk", ctypes.c_int), ("a_nsplit", ctypes.c_int), ("a_ws", P),
         ("a_cnt", P), ("a_out", P),
-        ("wbf16", ctypes.c_int), ("shard0", ctypes.c_int), ("shard_n", ctypes.c_int),
+        ("wbf16", ctypes.c_int), ("shard0", ctypes.c_int), ("shard_n", ctypes.c_int), ("xrank", ctypes.c_int),
+        ("cstride", ctypes.c_int),
     ]
 
 
@@ -144,10 +145,6 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
     def _create_program(self, stages):
         return create_program(stages)
 
-    def _shard(self, kind: str, total: int):
-        """(shard0, shard_n) of a stage for this rank: the whole stage on one GPU."""
-        return 0, 0
-
     def _pack_all(self):
         w = self.w
         mats = [w["lm_head"]]
@@ -182,7 +179,6 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
         if pro == PRO_EMBED_NORM:
             st.token = self.token.data_ptr()
             st.x_rows = self.cfg.vocab_size
-        st.shard0, st.shard_n = self._shard("tiles", sum((self._rows(sg) + 31) // 32 for sg in segs))
         if pro == PRO_SLICES_NORM:
             st.sl_in = self.sl_buf.data_ptr()
             st.sl_in_count = 0
@@ -193,10 +189,6 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
         for i, sg in enumerate(segs):
             st.seg[i] = sg
         return st
-
-    @staticmethod
-    def _rows(sg) -> int:
-        return int(sg.n)
 
     def _seg(self, m, epi, y=None, w2=None, aux0=None, aux1=None, aux2=None, cw=0, row_offset=0):
         s = StepSeg()
@@ -228,7 +220,6 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
         a.a_chunk, a.a_nsplit = self.attn_chunk, self.attn_nsplit
         a.a_ws, a.a_cnt = self.attn_ws.data_ptr(), self.attn_cnt.data_ptr()
         a.a_out = self.attn_out.data_ptr()
-        a.shard0, a.shard_n = self._shard("kv", cfg.num_key_value_heads)
         return a
 
     def _gdn_stage(self, i, ly):
@@ -246,7 +237,6 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
         g.g_heads = cfg.linear_num_value_heads
         g.g_dim = cfg.linear_value_head_dim
         g.g_rep = cfg.linear_num_value_heads // cfg.linear_num_key_heads
-        g.shard0, g.shard_n = self._shard("heads", cfg.linear_num_value_heads)
         return g
 
     def _build_stages(self):

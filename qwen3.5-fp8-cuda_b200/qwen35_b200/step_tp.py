@@ -1,24 +1,34 @@
 """Tensor-parallel decode on the persistent step kernel: one process and one
-cooperative launch per GPU per token.
+cooperative launch per GPU per token (`qwen_step_create_tp`,
+include/qwen_step.h).
 
-Every stage of the step is split over the ranks (`qwen_step_create_tp`,
-include/qwen_step.h): GEMV stages by 32-row tiles of their output (the
-LM head and every projection and MLP matrix shard by output rows, the
-residual projections keep their K slices), GatedDeltaNet by value heads and
-attention by KV heads (with 8 ranks and 4 KV heads, ranks r and r + 4 compute
-the same head).  Each CTA stores its outputs on every rank over NVLink and
-arrives on every rank's stage counter, so a rank's next stage reads a
-complete, local input vector - the all-gather of the row-parallel outputs is
-the stores themselves, and the greedy argmax is reduced by every CTA folding
-its packed (logit, index) key into every rank's workspace.  Waits read local
-memory only.
+Per layer, rank r of W takes (column- then row-parallel, so only two of the
+five stages exchange data between GPUs):
 
-The buffers that stages write (stage outputs, K slices, token, key, position,
-argmax workspace, logits and the stage counters) live in one arena per rank
-with the same layout on every rank, allocated with `qwen_ipc_alloc` and
-mapped by the peers through CUDA IPC (handles exchanged over the process
-group).  Everything else (weights, caches, recurrent state, the residual
-stream) is per rank; the weights are identical on every rank.
+* in_proj: the q / k / v / z rows of its GatedDeltaNet heads (value heads
+  [32 r / W, 32 (r + 1) / W) and their key heads; the 32-row a / b
+  projections are computed whole on every rank), or q / k / v: the rows of
+  its attention KV heads (with 8 ranks and 4 KV heads, ranks r and r + 4
+  compute the same head); the GatedDeltaNet / attention stage then has all
+  its inputs on its own GPU;
+* out_proj / o_proj: the K range of its heads for every output row, as FP32
+  K-slice rows stored into slots [r x nslice, (r + 1) x nslice) of every
+  rank's slice buffer over NVLink as tagged words (value | step-and-stage
+  tag); the next stage polls the words for the tag instead of waiting on a
+  counter;
+* gate/up: a 512-aligned range of the intermediate rows; down: the same
+  range of K for every row (K-slice rows to every rank, as above);
+* the next stage's prologue sums the W x nslice slices in rank order, so
+  every rank holds the same residual stream;
+* LM head: a range of vocabulary rows; every CTA folds its packed (logit,
+  index) key into every rank's workspace and each rank's CTA 0 finalises.
+
+The buffers written across GPUs (slices, logits, argmax workspace, token,
+key, position, counters) live in an arena with the same layout on every rank,
+allocated with `qwen_ipc_alloc` and mapped by the peers through CUDA IPC;
+everything else is per rank.  Every output row is computed with the same
+chunk order as on one GPU, so with the same K-slice arithmetic the results
+are bit-identical to the single-GPU engine's.
 """
 
 from __future__ import annotations
@@ -29,7 +39,10 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .step import P, Qwen35StepEngine, StepStage
+from .step import (EPI_ARGMAX, EPI_CONV, EPI_GATE_BETA, EPI_GATE_G, EPI_SILU_PAIR, EPI_SLICES, EPI_STORE, P,
+                   PRO_EMBED_NORM, PRO_PLAIN, PRO_SLICES_NORM, Qwen35StepEngine, StepStage)
+
+CHUNK_K, CHUNK_BYTES, TILE_ROWS = 512, 16400, 32
 
 
 class _DevArray:
@@ -65,23 +78,157 @@ class Qwen35StepTPEngine(Qwen35StepEngine):
         super().__init__(cfg, weights, **kw)
 
     # ------------------------------------------------------------------
-    def _shard(self, kind: str, total: int):
-        W, r = self.world, self.rank
-        if W == 1:
-            return 0, 0
-        if kind == "kv" and total < W:  # more ranks than KV heads: ranks r and r + total share a head
-            return r % total, 1
-        lo, hi = r * total // W, (r + 1) * total // W
+    def _split(self, total: int, what: str):
+        """This rank's [lo, hi) of `total` units (contiguous, in rank order)."""
+        lo, hi = self.rank * total // self.world, (self.rank + 1) * total // self.world
         if hi <= lo:
-            raise ValueError(f"{kind}: {total} units cannot be split over {W} ranks")
-        return lo, hi - lo
+            raise ValueError(f"{what}: {total} units cannot be split over {self.world} ranks")
+        return lo, hi
+
+    @staticmethod
+    def _sub(seg, m, r0: int, r1: int):
+        """Restrict `seg` (built over all rows of matrix `m`) to rows [r0, r1):
+        the packed weights start at tile r0 / 32, the outputs and per-row
+        epilogue operands at row r0."""
+        if r0 % TILE_ROWS or r1 <= r0:
+            raise ValueError(f"row range [{r0}, {r1}) is not a 32-row-aligned range")
+        wt = m[0] if isinstance(m, tuple) else m
+        C = wt.shape[1] // (CHUNK_K if isinstance(m, tuple) else 256)
+        off = (r0 // TILE_ROWS) * C * CHUNK_BYTES
+        seg.w += off
+        if seg.w2:
+            seg.w2 += off
+        seg.n = r1 - r0
+        if seg.y:
+            seg.y += (4 if seg.epi == EPI_GATE_G else 2) * r0
+        if seg.epi == EPI_CONV:  # conv1d weights and conv state: cw BF16 values per channel
+            seg.aux0 += 2 * r0 * seg.cw
+            seg.aux2 += 2 * r0 * seg.cw
+        elif seg.epi == EPI_GATE_G:  # A_log, dt_bias: FP32 per head
+            seg.aux0 += 4 * r0
+            seg.aux1 += 4 * r0
+        elif seg.epi == EPI_ARGMAX:
+            seg.row_offset += r0
+        return seg
+
+    def _row_parallel(self, m, x, sl, c0: int, c1: int):
+        """Chunks [c0, c1) of K of every row of `m`: FP32 K-slice rows into
+        slots [rank x nslice, (rank + 1) x nslice) of `sl` on every rank."""
+        C = m[0].shape[1] // CHUNK_K
+        seg = self._seg(m, EPI_SLICES)
+        seg.w += c0 * CHUNK_BYTES
+        st = self._gemv((c1 - c0) * CHUNK_K, PRO_PLAIN, [seg], x=x, nslice=self.nslice)
+        st.x += 2 * c0 * CHUNK_K
+        st.sl_out, st.sl_rows = sl.data_ptr(), self.cfg.hidden_size
+        st.xrank, st.cstride = 1, C
+        return st
+
+    def _k_chunks(self, lo: int, hi: int, what: str):
+        if lo % CHUNK_K or hi % CHUNK_K:
+            raise ValueError(f"{what}: K range [{lo}, {hi}) of rank {self.rank} is not 512-aligned")
+        return lo // CHUNK_K, hi // CHUNK_K
+
+    def _build_stages(self):
+        if self.world == 1:
+            return super()._build_stages()
+        cfg, w, W, r = self.cfg, self.w, self.world, self.rank
+        H = cfg.hidden_size
+        stages = []
+
+        def with_slices(st, sl):
+            st.sl_in, st.sl_in_count, st.sl_stride = sl.data_ptr(), 0, H
+            return st
+
+        for i, ly in enumerate(w["layers"]):
+            if i == 0:
+                inp = dict(pro=PRO_EMBED_NORM, x=w["embed"], h_out=self.hidden, norm_w=ly["input_layernorm"])
+            else:
+                inp = dict(pro=PRO_SLICES_NORM, res=self.h2, h_out=self.hidden, norm_w=ly["input_layernorm"])
+            if cfg.layer_types[i] == "full_attention":
+                nh, nkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+                G = nh // nkv
+                if W <= nkv:
+                    kh0, kh1 = self._split(nkv, "KV heads")
+                    qh0, qh1 = kh0 * G, kh1 * G
+                else:  # W / nkv ranks share a KV head and split its query heads for o_proj
+                    per = W // nkv
+                    if W % nkv or G % per:
+                        raise ValueError(f"{nkv} KV heads x {G} query heads cannot be split over {W} ranks")
+                    kh0, kh1 = r // per, r // per + 1
+                    qh0 = kh0 * G + (r % per) * (G // per)
+                    qh1 = qh0 + G // per
+                segs = [self._sub(self._seg(ly["q_proj"], EPI_STORE, y=self.q_all), ly["q_proj"],
+                                  kh0 * G * 2 * hd, kh1 * G * 2 * hd),
+                        self._sub(self._seg(ly["k_proj"], EPI_STORE, y=self.k_new), ly["k_proj"], kh0 * hd, kh1 * hd),
+                        self._sub(self._seg(ly["v_proj"], EPI_STORE, y=self.v_new), ly["v_proj"], kh0 * hd, kh1 * hd)]
+                st = self._gemv(H, segs=segs, **inp)
+                stages.append(with_slices(st, self.sl_buf2) if i else st)
+                a = self._attn_stage(i, ly)
+                a.shard0, a.shard_n = kh0, kh1 - kh0
+                stages.append(a)
+                c0, c1 = self._k_chunks(qh0 * hd, qh1 * hd, "o_proj")
+                stages.append(self._row_parallel(ly["o_proj"], self.attn_out, self.sl_buf, c0, c1))
+            else:
+                nv, nk = cfg.linear_num_value_heads, cfg.linear_num_key_heads
+                dk, dv, rep = cfg.linear_key_head_dim, cfg.linear_value_head_dim, nv // nk
+                kd = nk * dk
+                hv0, hv1 = self._split(nv, "value heads")
+                if hv0 % rep or hv1 % rep:
+                    raise ValueError(f"{nv} value heads over {nk} key heads cannot be split over {W} ranks")
+                hk0, hk1 = hv0 // rep, hv1 // rep
+                qkv = ly["in_proj_qkv"]
+
+                def conv(r0, r1):
+                    s = self._seg(qkv, EPI_CONV, y=self.qkv_conv, aux0=ly["conv1d_w"], aux2=self.conv_state[i],
+                                  cw=cfg.linear_conv_kernel_dim)
+                    return self._sub(s, qkv, r0, r1)
+
+                segs = [conv(hk0 * dk, hk1 * dk), conv(kd + hk0 * dk, kd + hk1 * dk),
+                        conv(2 * kd + hv0 * dv, 2 * kd + hv1 * dv),
+                        self._sub(self._seg(ly["in_proj_z"], EPI_STORE, y=self.z), ly["in_proj_z"], hv0 * dv,
+                                  hv1 * dv),
+                        # the per-head gates (one row per value head) are computed whole on every rank
+                        self._seg(ly["in_proj_a"], EPI_GATE_G, y=self.g, aux0=ly["A_log"], aux1=ly["dt_bias"]),
+                        self._seg(ly["in_proj_b"], EPI_GATE_BETA, y=self.beta)]
+                st = self._gemv(H, segs=segs, **inp)
+                stages.append(with_slices(st, self.sl_buf2) if i else st)
+                g = self._gdn_stage(i, ly)
+                g.shard0, g.shard_n = hv0, hv1 - hv0
+                stages.append(g)
+                c0, c1 = self._k_chunks(hv0 * dv, hv1 * dv, "out_proj")
+                stages.append(self._row_parallel(ly["out_proj"], self.attn_out, self.sl_buf, c0, c1))
+            # MLP: a 512-aligned range of the intermediate rows, then the same K range of down
+            c0, c1 = self._split(cfg.intermediate_size // CHUNK_K, "intermediate chunks")
+            gu = self._sub(self._seg(ly["gate_proj"], EPI_SILU_PAIR, y=self.silu, w2=ly["up_proj"]), ly["gate_proj"],
+                           c0 * CHUNK_K, c1 * CHUNK_K)
+            stages.append(with_slices(self._gemv(H, PRO_SLICES_NORM, [gu], res=self.hidden, h_out=self.h2,
+                                                 norm_w=ly["post_attention_layernorm"], pair=1), self.sl_buf))
+            stages.append(self._row_parallel(ly["down_proj"], self.silu, self.sl_buf2, c0, c1))
+        V = cfg.vocab_size
+        t0, t1 = self._split((V + TILE_ROWS - 1) // TILE_ROWS, "LM-head tiles")
+        lm = w["lm_head"]
+        seg = self._sub(self._seg(lm, EPI_ARGMAX, y=self.logits), lm, t0 * TILE_ROWS, min(t1 * TILE_ROWS, V))
+        head = with_slices(self._gemv(H, PRO_SLICES_NORM, [seg], res=self.h2, h_out=self.hidden, norm_w=w["norm_f"]),
+                           self.sl_buf2)
+        head.wbf16 = 0 if isinstance(lm, tuple) else 1
+        head.am_ws = self.am_ws.data_ptr()
+        head.am_key_out = self.key.data_ptr()
+        head.am_token_out = self.token.data_ptr()
+        head.pos_inc = self.pos.data_ptr()
+        stages.append(head)
+        return (StepStage * len(stages))(*stages)
 
     def _setup_shared(self):
         """Move every buffer a stage writes into the IPC arena and map the peers'."""
         cfg, dev = self.cfg, self.device
         lib = self.lib
-        names = ["q_all", "k_new", "v_new", "attn_out", "qkv_conv", "z", "g", "beta", "silu", "sl_buf", "token",
-                 "key", "pos", "am_ws"] + (["logits"] if self.logits is not None else [])
+        # K-slice buffers of tagged 8-byte words (16 slots x hidden each, zero:
+        # no tag); down writes the second while the other ranks may still read
+        # out_proj's / o_proj's from the first
+        H = cfg.hidden_size
+        self.sl_buf = torch.zeros(2 * self.sl_max * H, dtype=torch.float32, device=dev)
+        self.sl_buf2 = torch.zeros_like(self.sl_buf)
+        names = ["sl_buf", "sl_buf2", "token", "key", "pos", "am_ws"] + (["logits"] if self.logits is not None else [])
         nstages = 5 * cfg.num_hidden_layers + 1
         layout, off = {}, 0
         for name in names:

@@ -1,6 +1,8 @@
 """Tensor-parallel step kernel on 2, 4 and 8 GPUs of one box (each skipped with
 fewer GPUs): tests/step_tp_worker.py under torch.distributed.run; greedy
-tokens and logits must be bit-identical to the single-GPU step engine's."""
+tokens and logits bit-identical to the single-GPU step engine's where the
+K-slice order can match, else within the distance of two single-GPU
+summation orders."""
 
 import os
 import subprocess
