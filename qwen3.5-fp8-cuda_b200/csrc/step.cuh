@@ -466,7 +466,7 @@ __device__ __forceinline__ float4 st_slice4(const float* sl, size_t idx, bool ta
 // the 128-blocks warp, warp + 8, ... of K) carries `tag`: all tags loaded at
 // once, the whole set again while any is missing (bounded by the wait limit
 // and the abort flag; on time-out the step is abandoned with error 8).
-__device__ __noinline__ void st_ll_wait_all(const unsigned long long* sl, int nsl, int stride, int nb, uint32_t tag,
+__device__ __forceinline__ void st_ll_wait_all(const unsigned long long* sl, int nsl, int stride, int nb, uint32_t tag,
                                             unsigned* abort_flag) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint64_t t0 = 0;
@@ -516,7 +516,6 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   float4 wv[MB];
   float4 sp[MB][SLR > 0 ? SLR : 1];
   const int nreg = pro == STP_SLICES_NORM ? (nsl < SLR ? nsl : SLR) : 0;
-  if (ll) st_ll_wait_all(reinterpret_cast<const unsigned long long*>(sl_in), nsl, sl_stride, nb, ll_tag, abort_flag);
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
     const int b = warp + i * ST_CW;
@@ -525,6 +524,15 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
       raw[i] = pro == STP_EMBED_NORM ? __ldg(reinterpret_cast<const uint2*>(src + k0))
                                      : __ldcg(reinterpret_cast<const uint2*>(src + k0));
       if (norm) wv[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k0));
+    }
+  }
+  // (the residual and norm loads above are in flight while the tags are polled)
+  if (ll) st_ll_wait_all(reinterpret_cast<const unsigned long long*>(sl_in), nsl, sl_stride, nb, ll_tag, abort_flag);
+#pragma unroll
+  for (int i = 0; i < MB; ++i) {
+    const int b = warp + i * ST_CW;
+    const int k0 = b * 128 + lane * 4;
+    if (b < nb) {
 #pragma unroll
       for (int c = 0; c < SLR; ++c)
         if (c < nreg) sp[i][c] = st_slice4(sl_in, (size_t)c * sl_stride + k0, ll);
