@@ -6,21 +6,27 @@
 // called by fp8_linear main.py:262-269 during prefill).  FP8 MMAs with the
 // weights exactly as stored and a per-128-K-block scale promotion in FP32:
 //
-//   * gemm_x_split_kernel turns x into the B operand once per call: for every
-//     token tile of 64 rows a [128, K] E4M3 block whose rows 0-63 hold
-//     hi = RN(x * 2^e) and rows 64-127 hold lo = RN(32 (x * 2^e - hi)), with
-//     e per (token, 128-K block) chosen so that the block's largest magnitude
-//     lands in [2^7, 2^8) (hi + lo / 32 equals the BF16 value for every
-//     element within 2^-14 of that maximum), plus 2^-e per (token, block).
+//   * gemm_x_split_kernel turns x into the A operand once per call: for every
+//     token tile of 64 rows a [128, K] E4M3 block; token 16 g + j (g < 4,
+//     j < 16) has hi = RN(x * 2^e) in row 32 g + j and lo = RN(32 (x * 2^e -
+//     hi)) in row 32 g + 16 + j, with e per (token, 128-K block) chosen so
+//     that the block's largest magnitude lands in [2^7, 2^8) (hi + lo / 32
+//     equals the BF16 value for every element within 2^-14 of that maximum),
+//     plus 2^-e per (token, block).
 //   * gemm_tc_kernel walks (128 weight rows) x (64 tokens) output tiles,
 //     weight-row-major so that consecutive tiles reuse the weight tile from
-//     L2.  Warp 0 streams A (weights) and B (split x) K-blocks with 2-D TMA
-//     (128-byte swizzle) into a ring of 32 KB stages; warp 1 issues four
+//     L2.  Warp 0 streams the split x (A) and weight (B) K-blocks with 2-D
+//     TMA (128-byte swizzle) into a ring of 32 KB stages; warp 1 issues four
 //     tcgen05.mma kind::f8f6f4 (M=128, N=128, K=32) per K-block into one of
-//     two TMEM accumulators; eight epilogue warps (two per TMEM lane quarter,
-//     32 tokens each) read the finished K-block, add hi + lo / 32 times
-//     scale[n/128, kb] * 2^-e[token, kb] into FP32 registers and, at the end
-//     of the tile, store BF16 y.
+//     two TMEM accumulators, whose lanes are then split-x rows and whose
+//     columns are weight rows.  A K-block's scale scale[n/128, kb] *
+//     2^-e[token, kb] is one number per TMEM lane (the weight block covers all
+//     128 columns), so each of the eight epilogue warps (one TMEM lane quarter
+//     = 16 tokens' hi and lo rows, one 64-column half) adds its 64 columns
+//     times that number into FP32 registers: one FMA per accumulator element
+//     and K-block.  At the end of the tile the hi and lo lanes of a token
+//     exchange their sums (one shuffle per column), form hi + lo / 32 and
+//     store BF16 y.
 // Every mbarrier wait is bounded (QWEN_WAIT_TIMEOUT_NS) and reports a timeout
 // through the device error word.
 #pragma once
@@ -67,10 +73,29 @@ __global__ void __launch_bounds__(256) gemm_x_split_kernel(const bf16* __restric
   const uint32_t l01 = f32x2_to_e4m3x2((s[0] - g01.x) * 32.f, (s[1] - g01.y) * 32.f);
   const uint32_t l23 = f32x2_to_e4m3x2((s[2] - g23.x) * 32.f, (s[3] - g23.y) * 32.f);
   const int t = m / GM_TOK, r = m - t * GM_TOK;
+  const int row_hi = (r >> 4) * 32 + (r & 15);  // lo: row_hi + 16 (same TMEM lane quarter)
   uint8_t* tile = xs + (size_t)t * 128 * K;
-  *reinterpret_cast<uint32_t*>(tile + (size_t)r * K + kb * 128 + lane * 4) = h01 | (h23 << 16);
-  *reinterpret_cast<uint32_t*>(tile + (size_t)(GM_TOK + r) * K + kb * 128 + lane * 4) = l01 | (l23 << 16);
+  *reinterpret_cast<uint32_t*>(tile + (size_t)row_hi * K + kb * 128 + lane * 4) = h01 | (h23 << 16);
+  *reinterpret_cast<uint32_t*>(tile + (size_t)(row_hi + 16) * K + kb * 128 + lane * 4) = l01 | (l23 << 16);
   if (lane == 0) xinv[(size_t)m * nkb + kb] = exp2i(-e);
+}
+
+// 32 consecutive TMEM columns of this warp's lane quarter (one 32-bit value
+// per column and lane).
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&p);
 }
 
 struct GemmArgs {
@@ -164,8 +189,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t ad = tc_smem_desc(ring + (uint32_t)s * GM_STAGE);
-          const uint64_t bd = tc_smem_desc(ring + (uint32_t)s * GM_STAGE + TC_TILE);
+          // A = the split x tile (lanes: x rows), B = the weight tile (columns: weight rows)
+          const uint64_t ad = tc_smem_desc(ring + (uint32_t)s * GM_STAGE + TC_TILE);
+          const uint64_t bd = tc_smem_desc(ring + (uint32_t)s * GM_STAGE);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             asm volatile(
@@ -182,62 +208,68 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
     __syncwarp();
   } else if (warp >= 4) {
-    // ---------------- epilogue: 8 warps, lane quarter q, token half h ----------------
+    // ---------------- epilogue: 8 warps, lane quarter q, column half h ----------------
     pdl_wait();  // xinv comes from the previous kernel; y may still be read by it
     const int q = warp & 3, h = (warp - 4) >> 2;
-    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 64);
+    const bool lo_lane = lane >= 16;
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const int n0 = (t / ntm) * TC_ROWS, m0 = (t % ntm) * GM_TOK + h * 32;
-      const int n = n0 + q * 32 + lane;
+      const int n0 = (t / ntm) * TC_ROWS + h * 64, m = (t % ntm) * GM_TOK + q * 16 + (lane & 15);
       const int srow = (n0 >> 7) * nkb;
-      float acc[32];
+      const float* xi_row = a.xinv + (size_t)m * nkb;
+      float acc[64];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+      for (int j = 0; j < 64; ++j) acc[j] = 0.f;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int b = it & 1;
-        // this lane's token's 2^-e for this block (broadcast below), and the block scale
-        const float xi = a.xinv[(size_t)(m0 + lane) * nkb + kb];
-        const float sw = load_scale<ST>(a.s, srow + kb);
+        // this lane's scale for the block: the token's 2^-e times the weight block's scale
+        const float f = xi_row[kb] * load_scale<ST>(a.s, srow + kb);
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(tfull_bar(b), (it >> 1) & 1));
         if (!ok) continue;
         tc_fence_after();
-        uint32_t vh[32], vl[32];
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(vh[0]), "=r"(vh[1]), "=r"(vh[2]), "=r"(vh[3]), "=r"(vh[4]), "=r"(vh[5]), "=r"(vh[6]), "=r"(vh[7]),
-              "=r"(vh[8]), "=r"(vh[9]), "=r"(vh[10]), "=r"(vh[11]), "=r"(vh[12]), "=r"(vh[13]), "=r"(vh[14]),
-              "=r"(vh[15]), "=r"(vh[16]), "=r"(vh[17]), "=r"(vh[18]), "=r"(vh[19]), "=r"(vh[20]), "=r"(vh[21]),
-              "=r"(vh[22]), "=r"(vh[23]), "=r"(vh[24]), "=r"(vh[25]), "=r"(vh[26]), "=r"(vh[27]), "=r"(vh[28]),
-              "=r"(vh[29]), "=r"(vh[30]), "=r"(vh[31])
-            : "r"(tl + b * 128 + h * 32)
-            : "memory");
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(vl[0]), "=r"(vl[1]), "=r"(vl[2]), "=r"(vl[3]), "=r"(vl[4]), "=r"(vl[5]), "=r"(vl[6]), "=r"(vl[7]),
-              "=r"(vl[8]), "=r"(vl[9]), "=r"(vl[10]), "=r"(vl[11]), "=r"(vl[12]), "=r"(vl[13]), "=r"(vl[14]),
-              "=r"(vl[15]), "=r"(vl[16]), "=r"(vl[17]), "=r"(vl[18]), "=r"(vl[19]), "=r"(vl[20]), "=r"(vl[21]),
-              "=r"(vl[22]), "=r"(vl[23]), "=r"(vl[24]), "=r"(vl[25]), "=r"(vl[26]), "=r"(vl[27]), "=r"(vl[28]),
-              "=r"(vl[29]), "=r"(vl[30]), "=r"(vl[31])
-            : "r"(tl + b * 128 + GM_TOK + h * 32)
-            : "memory");
+        uint32_t v0[32], v1[32];
+        tc_ld32(tl + b * 128, v0);
+        tc_ld32(tl + b * 128 + 32, v1);
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(tempty_bar(b));
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float f = __shfl_sync(0xffffffffu, xi, j) * sw;
-          acc[j] = fmaf(__uint_as_float(vh[j]) + __uint_as_float(vl[j]) * 0.03125f, f, acc[j]);
+          acc[j] = fmaf(__uint_as_float(v0[j]), f, acc[j]);
+          acc[32 + j] = fmaf(__uint_as_float(v1[j]), f, acc[32 + j]);
         }
       }
-      if (n < a.N) {
+      // hi + lo / 32: lanes j and j + 16 hold the same token's hi and lo sums;
+      // lane j stores columns [0, 32), lane j + 16 columns [32, 64)
+      float y[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (m0 + j < a.M) a.y[(size_t)(m0 + j) * a.N + n] = f2bf(acc[j]);
+      for (int j = 0; j < 32; ++j) {
+        const float mine_a = acc[j], mine_b = acc[32 + j];
+        const float other_a = __shfl_xor_sync(0xffffffffu, mine_a, 16);
+        const float other_b = __shfl_xor_sync(0xffffffffu, mine_b, 16);
+        y[j] = lo_lane ? other_b + mine_b * 0.03125f : mine_a + other_a * 0.03125f;
+      }
+      const int c0 = n0 + (lo_lane ? 32 : 0);
+      if (m < a.M) {
+        bf16* dst = a.y + (size_t)m * a.N + c0;
+        if (c0 + 32 <= a.N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 pk;
+            pk.x = pack_bf16x2(y[j], y[j + 1]);
+            pk.y = pack_bf16x2(y[j + 2], y[j + 3]);
+            pk.z = pack_bf16x2(y[j + 4], y[j + 5]);
+            pk.w = pack_bf16x2(y[j + 6], y[j + 7]);
+            *reinterpret_cast<uint4*>(dst + j) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < a.N) dst[j] = f2bf(y[j]);
+        }
       }
     }
     if (!ok) qwen_err_set(ERR_TC_TIMEOUT);
