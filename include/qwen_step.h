@@ -52,6 +52,7 @@ extern "C" {
 #define QWEN_STEP_EPI_GATE_G 5     /* y(f32)[r] = -exp(A_log[r]) * softplus(bf16(v) + dt_bias[r]) */
 #define QWEN_STEP_EPI_GATE_BETA 6  /* y[r] = bf16(sigmoid(bf16(v))) */
 #define QWEN_STEP_EPI_SLICES 9     /* FP32 partial rows into the stage's sl_out [nslice][sl_rows] */
+#define QWEN_STEP_EPI_SILU 10      /* y[r] = bf16(silu(bf16(v))) */
 
 typedef struct qwen_step_seg {
   const void* w;         /* packed weights (qwen_step_pack) */
@@ -98,9 +99,13 @@ typedef struct qwen_step_stage {
   const void* g_v;       /* BF16 [value heads][128] */
   const float* g_g;      /* FP32 [value heads] log-decay */
   const void* g_beta;    /* BF16 [value heads] */
-  float* g_state;        /* FP32 [value heads][128][128], in place */
-  void* g_out;           /* BF16 [value heads][128] */
-  const void* g_z;       /* gated RMSNorm: BF16 [value heads][128] (null: core output) */
+  float* g_state;        /* FP32 [value heads][4][128 keys][32 values] (value block b holds
+                            columns 32 b .. 32 b + 31 of the [keys][values] state), in place */
+  void* g_out;           /* BF16 [value heads][128]: the core output */
+  const void* g_z;       /* gated RMSNorm: BF16 silu(z) [value heads][128] (an EPI_SILU
+                            output; null: none).  The norm is
+                            applied by the next stage, which must be a PLAIN GEMV whose x is
+                            whole heads of g_out (K <= 4096): its prologue normalises them */
   const void* g_norm_w;  /* BF16 [128] */
   float g_eps;
   int g_heads;

@@ -63,6 +63,7 @@ enum GemvEpi : int {
   EPI_F32_P2P = 8,    // v into slot [rank] of every rank's exchange buffer (aux0 = P2PTable*)
   EPI_SLICES = 9,     // y(f32)[slice * n + r] = this K slice's partial v; y2 (int*) = slice count
                       // (tensor-core kernel, one segment: the next launch adds the slices)
+  EPI_SILU = 10,      // y[r] = bf16(silu(bf16(v))) (step kernel: the GatedDeltaNet output gate)
 };
 
 enum GemvPro : int {

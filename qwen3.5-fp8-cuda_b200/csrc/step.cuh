@@ -90,14 +90,21 @@ constexpr int ST_BATCH = 48;                   // chunk partials held before a r
 constexpr int ST_MAX_SEG = 6;
 constexpr int ST_ATTN_SLOTS = QWEN_STEP_ATTN_SLOTS;  // contiguous ring slots of scratch for an attention unit
 constexpr int ST_GDN_D = 128;                  // GatedDeltaNet head dim of the step kernel
-constexpr int ST_GDN_SLOTS = ST_GDN_D * ST_GDN_D * 4 / ST_WBYTES;  // 4: one head's FP32 state
-constexpr int ST_GDN_KPS = ST_WBYTES / (ST_GDN_D * 4);            // 32 key rows of state per slot
+// A GatedDeltaNet unit is one block of ST_GDN_DC value columns of one head:
+// its FP32 state [D keys][DC values] is one contiguous ring slot (the step
+// kernel's state layout is [head][value block][key][DC]).
+constexpr int ST_GDN_VS = 4;
+constexpr int ST_GDN_DC = ST_GDN_D / ST_GDN_VS;  // 32
+constexpr int ST_GDN_KG = ST_NT / ST_GDN_DC;     // 8 key groups (a thread: one column, KR keys)
+constexpr int ST_GDN_KR = ST_GDN_D / ST_GDN_KG;  // 16
+constexpr int ST_GATED_MAXB = 4096 / 128 / ST_CW;  // 128-blocks per warp of a gated prologue (K <= 4096)
+static_assert(ST_GDN_D * ST_GDN_DC * 4 == ST_WBYTES, "a GatedDeltaNet unit's state is one ring slot");
+static_assert(ST_GDN_KG * ST_GDN_KR == ST_GDN_D && ST_GDN_KG == 8, "key groups");
 static_assert(ST_SLOTS % ST_PAIRS == 0, "items m and m + ST_SLOTS must go to the same consumer warp pair");
 static_assert(ST_SLOTS % ST_ATTN_SLOTS == 0, "attention scratch groups must not wrap the ring");
 // an attention unit waits for its alignment padding plus its scratch slots at
 // once (up to 2 * ST_ATTN_SLOTS - 1 items): they must fit the ring together
 static_assert(2 * ST_ATTN_SLOTS - 1 <= ST_SLOTS, "attention padding + scratch must fit the ring");
-static_assert(ST_GDN_SLOTS <= ST_SLOTS, "a head's state must fit the ring");
 static_assert(ST_NT == ATTN_WARPS * 32, "attention units run on the consumer warps");
 
 
@@ -142,7 +149,15 @@ struct alignas(16) StStage {
   // SLICES_NORM prologue: index of the xrank stage whose tagged slices it
   // sums (polled until they carry that stage's tag of this step), or -1
   int sl_src;
-  int pad_;
+  // PLAIN prologue over a GatedDeltaNet stage's core output (x): the gated
+  // RMSNorm of every 128-wide block (one head) is applied first,
+  // bf16(bf16(bf16(c / rms(c)) w) zs), with zs = bf16(silu(z)) at gz (same
+  // layout as x) and the head's norm weights gnw [128]
+  int gated_pro;
+  const bf16* gz;
+  const bf16* gnw;
+  float geps;
+  int pad_[3];
 };
 
 // Shared memory plan (bytes from the dynamic shared memory base).
@@ -398,17 +413,16 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
         }
       }
     } else if (S.kind == ST_GDN) {
-      st_range(S.gdn_heads, u0, u1);
+      // one slot per (head, value block): that block's state
+      st_range(S.gdn_heads * ST_GDN_VS, u0, u1);
       const uint8_t* state = reinterpret_cast<const uint8_t*>(S.gdn.state);
-      for (int h = u0; h < u1 && ok; ++h) {
-        const uint8_t* src = state + (size_t)(S.shard0 + h) * ST_GDN_D * ST_GDN_D * 4;
-        for (int i = 0; i < ST_GDN_SLOTS; ++i) {
-          uint32_t slot;
-          if (!(ok = acquire(slot))) break;
-          mbar_arrive_expect_tx(full0 + 8 * slot, ST_WBYTES);
-          bulk_g2s(ring + slot * ST_CHUNK, src + (size_t)i * ST_WBYTES, ST_WBYTES, full0 + 8 * slot, pol);
-          ++n;
-        }
+      for (int u = u0; u < u1 && ok; ++u) {
+        const uint8_t* src = state + ((size_t)S.shard0 * ST_GDN_VS + u) * ST_WBYTES;
+        uint32_t slot;
+        if (!(ok = acquire(slot))) break;
+        mbar_arrive_expect_tx(full0 + 8 * slot, ST_WBYTES);
+        bulk_g2s(ring + slot * ST_CHUNK, src, ST_WBYTES, full0 + 8 * slot, pol);
+        ++n;
       }
     } else {  // ST_ATTN: scratch slots, no copy (a plain arrival completes the phase)
       st_range(S.attn_kv * S.attn.nsplit, u0, u1);
@@ -488,7 +502,7 @@ __device__ __forceinline__ void st_ll_wait_all(const unsigned long long* sl, int
   }
 }
 
-template <int MB, int SLR>
+template <int MB, int SLR, bool GATED = false>
 __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8_t* xl, float* xinv, float* red,
                                             uint32_t ll_tag, unsigned* abort_flag) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -515,6 +529,9 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   uint2 raw[MB];
   float4 wv[MB];
   float4 sp[MB][SLR > 0 ? SLR : 1];
+  uint2 zr[GATED ? MB : 1];
+  uint2 gw = make_uint2(0u, 0u);
+  if (GATED) gw = __ldg(reinterpret_cast<const uint2*>(S.gnw + lane * 4));  // a block is one head
   const int nreg = pro == STP_SLICES_NORM ? (nsl < SLR ? nsl : SLR) : 0;
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
@@ -524,6 +541,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
       raw[i] = pro == STP_EMBED_NORM ? __ldg(reinterpret_cast<const uint2*>(src + k0))
                                      : __ldcg(reinterpret_cast<const uint2*>(src + k0));
       if (norm) wv[i] = __ldg(reinterpret_cast<const float4*>(norm_w + k0));
+      if (GATED) zr[GATED ? i : 0] = __ldcg(reinterpret_cast<const uint2*>(S.gz + k0));
     }
   }
   // (the residual and norm loads above are in flight while the tags are polled)
@@ -543,6 +561,23 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   for (int i = 0; i < MB; ++i) {
     const float2 a01 = bf2x_to_f2(raw[i].x), a23 = bf2x_to_f2(raw[i].y);
     v[i][0] = a01.x; v[i][1] = a01.y; v[i][2] = a23.x; v[i][3] = a23.y;
+  }
+  if (GATED) {
+    // the GatedDeltaNet's gated RMSNorm per head (main.py:1152-1159):
+    // bf16(c / rms(c)), times the norm weight, times bf16(silu(z))
+    const float2 w01 = bf2x_to_f2(gw.x), w23 = bf2x_to_f2(gw.y);
+    const float nw[4] = {w01.x, w01.y, w23.x, w23.y};
+#pragma unroll
+    for (int i = 0; i < MB; ++i) {
+      const int b = warp + i * ST_CW;
+      const float cs = warp_sum(v[i][0] * v[i][0] + v[i][1] * v[i][1] + v[i][2] * v[i][2] + v[i][3] * v[i][3]);
+      if (b >= nb) continue;  // warp-uniform
+      const float inv = rsqrtf(cs / (float)ST_GDN_D + S.geps);
+      const float2 z01 = bf2x_to_f2(zr[GATED ? i : 0].x), z23 = bf2x_to_f2(zr[GATED ? i : 0].y);
+      const float zs[4] = {z01.x, z01.y, z23.x, z23.y};  // bf16(silu(z)), from in_proj's EPI_SILU
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[i][q] = bfround(bfround(bfround(v[i][q] * inv) * nw[q]) * zs[q]);
+    }
   }
   if (pro == STP_SLICES_NORM) {
     float sum[MB][4];
@@ -792,6 +827,10 @@ __device__ __forceinline__ unsigned long long st_epilogue(const StProgram& P, co
     case EPI_GATE_BETA:
       st_put_local(reinterpret_cast<bf16*>(sg.y) + r, f2bf(1.0f / (1.0f + expf(-bfround(v)))));
       break;
+    case EPI_SILU: {  // the gated RMSNorm's bf16(silu(z)) of the BF16 z row
+      const float z = bfround(v);
+      st_put_local(reinterpret_cast<bf16*>(sg.y) + r, f2bf(z / (1.0f + expf(-z))));
+    } break;
     default:
       break;
   }
@@ -878,7 +917,9 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int u0, u1;
   st_range(S.nunits, u0, u1);
-  if (S.pro == STP_PLAIN)
+  if (S.pro == STP_PLAIN && S.gated_pro)
+    st_prologue<ST_GATED_MAXB, 0, true>(S, X.xh, X.xl, X.xinv, X.red, 0u, X.abort_flag);
+  else if (S.pro == STP_PLAIN)
     st_prologue<ST_MAXB, 0>(S, X.xh, X.xl, X.xinv, X.red, 0u, X.abort_flag);
   else
     st_prologue<ST_NORM_MAXB, ST_SL_REG>(S, X.xh, X.xl, X.xinv, X.red, X.tag0 + (uint32_t)S.sl_src, X.abort_flag);
@@ -965,127 +1006,94 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
   if (S.am_ws) st_argmax_finish(*X.prog, S, am_best, X.misc);
 }
 
-// GatedDeltaNet step of one value head on the consumer warps: thread
-// (d = tid % 128, kg = tid / 128) keeps key rows [64 kg, 64 kg + 64) of value
-// column d in registers, read once from the ring (the state slots of the
-// head), and writes the updated column to global memory once.  Same
-// arithmetic as gdn_decode_kernel (the reference's delta_rule_decode_kernel,
-// fused_kernels.cu:623-684, plus the default path's gated RMSNorm,
-// main.py:1152-1159).
+// GatedDeltaNet step of one (value head, block of 32 value columns) unit on
+// the consumer warps: thread (d = tid % 32, kg = tid / 32) keeps key rows
+// [16 kg, 16 kg + 16) of value column 32 c + d in registers, read once from
+// the ring (the unit's state slot), and writes the updated column to global
+// memory once.  The arithmetic is the reference's delta_rule_decode_kernel
+// (fused_kernels.cu:623-684): L2-normalised q (times D^-1/2) and k, decay
+// exp(g), delta = (v - decay S^T k) beta, S' = decay S + k delta^T,
+// o = S'^T q.  The unit writes the core output bf16(o) of its 32 columns; the
+// default path's gated RMSNorm (main.py:1152-1159) needs the whole head and
+// is applied by the next GEMV's prologue (StStage::gated_pro).
 __device__ __forceinline__ void st_gdn(const StStage& S, const StCtx& X, uint32_t& n) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int D = ST_GDN_D;
+  constexpr int D = ST_GDN_D, DC = ST_GDN_DC, KG = ST_GDN_KG, KR = ST_GDN_KR;
   const GdnArgs& a = S.gdn;
   int u0, u1;
-  st_range(S.gdn_heads, u0, u1);
+  st_range(S.gdn_heads * ST_GDN_VS, u0, u1);
   float* qs = X.part;
   float* ks = X.part + D;
-  float* red2 = X.part + 2 * D;  // [2][D]
-  float* wsum = X.part + 4 * D;
-  for (int hu = u0; hu < u1; ++hu) {
-    const int h = S.shard0 + hu;  // this rank's heads
-    if (tid == 0) {
-      int ok = 1;
-      for (int i = 0; i < ST_GDN_SLOTS && ok; ++i) {
-        const uint32_t m = n + i;
-        if (!st_mbar_wait(X.full0 + 8 * (m % ST_SLOTS), (m / ST_SLOTS) & 1u, X.abort_flag)) ok = 0;
-      }
-      *X.flag = ok;
-    }
+  float* red2 = X.part + 2 * D;  // [KG][DC]
+  for (int u = u0; u < u1; ++u) {
+    const int h = S.shard0 + u / ST_GDN_VS, c = u % ST_GDN_VS;  // this rank's heads
+    const uint32_t slot = n % ST_SLOTS, par = (n / ST_SLOTS) & 1u;
+    if (tid == 0) *X.flag = st_mbar_wait(X.full0 + 8 * slot, par, X.abort_flag) ? 1 : 0;
     named_bar(1, ST_NT);
     if (*X.flag) {
-      // every thread observes the completed phases itself (acquire of the
-      // bulk-copied state); they have completed, so each wait returns at once
-      for (int i = 0; i < ST_GDN_SLOTS; ++i) {
-        const uint32_t m = n + i;
-        for (int it = 0; it < (1 << 16) && !mbar_try_wait(X.full0 + 8 * (m % ST_SLOTS), (m / ST_SLOTS) & 1u); ++it) {
-        }
+      // every thread observes the completed phase itself (acquire of the
+      // bulk-copied state); it has completed, so the wait returns at once
+      for (int it = 0; it < (1 << 16) && !mbar_try_wait(X.full0 + 8 * slot, par); ++it) {
       }
-      const int d = tid & (D - 1), kg = tid / D;
-      const int kh = h / a.rep;
-      // every global load of the head at once (one L2 round trip)
-      float qv = 0.f, kv = 0.f, zv = 0.f, nwv = 0.f;
-      if (tid < D) {
-        qv = bf2f(__ldcg(a.q + (size_t)kh * D + tid));
-        kv = bf2f(__ldcg(a.k + (size_t)kh * D + tid));
-        if (a.gated) {
-          zv = bf2f(__ldcg(a.z + (size_t)h * D + d));
-          nwv = bf2f(a.norm_w[d]);
-        }
-      }
+      const int d = tid % DC, kg = tid / DC, t = tid & (D - 1);
+      const int kh = h / a.rep, col = c * DC + d;
+      // every global load of the unit at once (one L2 round trip): q on
+      // warps 0-3, k on warps 4-7
+      const float qk = bf2f(__ldcg((tid < D ? a.q : a.k) + (size_t)kh * D + t));
       const float gval = __ldcg(a.g + h);
       const float bval = bf2f(__ldcg(a.beta + h));
-      const float vval = bf2f(__ldcg(a.v + (size_t)h * D + d));
-      const float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
-      if (lane == 0 && tid < D) {
-        X.red[warp] = sq;
-        X.red[4 + warp] = sk;
-      }
-      float s[64];
+      const float vval = bf2f(__ldcg(a.v + (size_t)h * D + col));
+      const float sq = warp_sum(qk * qk);
+      if (lane == 0) X.red[warp] = sq;
+      float s[KR];
+      const float* st = reinterpret_cast<const float*>(X.ring + slot * ST_CHUNK);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int k = kg * 64 + i;
-        const uint32_t slot = (n + k / ST_GDN_KPS) % ST_SLOTS;
-        s[i] = *reinterpret_cast<const float*>(X.ring + slot * ST_CHUNK + (k % ST_GDN_KPS) * (D * 4) + d * 4);
-      }
+      for (int i = 0; i < KR; ++i) s[i] = st[(kg * KR + i) * DC + d];
       named_bar(1, ST_NT);
       if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_PRO, (unsigned)globaltimer_ns());
       const float tq = X.red[0] + X.red[1] + X.red[2] + X.red[3];
       const float tk = X.red[4] + X.red[5] + X.red[6] + X.red[7];
-      const float q_scale = rsqrtf(tq + 1e-6f) * rsqrtf((float)D);
-      const float k_scale = rsqrtf(tk + 1e-6f);
-      if (tid < D) {
-        qs[tid] = qv * q_scale;
-        ks[tid] = kv * k_scale;
-      }
+      if (tid < D)
+        qs[t] = qk * (rsqrtf(tq + 1e-6f) * rsqrtf((float)D));
+      else
+        ks[t] = qk * rsqrtf(tk + 1e-6f);
       named_bar(1, ST_NT);
       const float decay = expf(gval);
-      const float beta = bval;
       float pred = 0.f;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) pred += s[i] * decay * ks[kg * 64 + i];
-      red2[kg * D + d] = pred;
+      for (int i = 0; i < KR; ++i) pred += s[i] * decay * ks[kg * KR + i];
+      red2[kg * DC + d] = pred;
       named_bar(1, ST_NT);
-      const float ptot = red2[d] + red2[D + d];
-      const float delta = (vval - ptot) * beta;
+      float ptot = 0.f;
+#pragma unroll
+      for (int g = 0; g < KG; ++g) ptot += red2[g * DC + d];
+      const float delta = (vval - ptot) * bval;
       named_bar(1, ST_NT);  // red2 is read before it is reused
       float o = 0.f;
-      float* Sg = a.state + (size_t)h * D * D;
+      float* Sg = a.state + ((size_t)h * ST_GDN_VS + c) * (D * DC);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int k = kg * 64 + i;
-        const float u = s[i] * decay + ks[k] * delta;
-        Sg[(size_t)k * D + d] = u;
-        o += u * qs[k];
+      for (int i = 0; i < KR; ++i) {
+        const int k = kg * KR + i;
+        const float v = s[i] * decay + ks[k] * delta;
+        Sg[k * DC + d] = v;
+        o += v * qs[k];
       }
-      red2[kg * D + d] = o;
+      red2[kg * DC + d] = o;
       named_bar(1, ST_NT);
       if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_CHUNKS, (unsigned)globaltimer_ns());
-      if (kg == 0) {
-        const bf16 core = f2bf(red2[d] + red2[D + d]);
-        bf16* out = a.out + (size_t)h * D + d;
-        if (!a.gated) {
-          *out = core;
-        } else {
-          const float c = bf2f(core);
-          const float cs = warp_sum(c * c);
-          if (lane == 0) wsum[warp] = cs;
-          named_bar(2, D);
-          const float var = (wsum[0] + wsum[1] + wsum[2] + wsum[3]) / (float)D;
-          const bf16 normed = f2bf(c * rsqrtf(var + a.eps));
-          const bf16 tv = f2bf(bf2f(normed) * nwv);
-          const bf16 zs = f2bf(zv / (1.0f + expf(-zv)));
-          *out = f2bf(bf2f(tv) * bf2f(zs));
-        }
+      if (tid < DC) {
+        float core = 0.f;
+#pragma unroll
+        for (int g = 0; g < KG; ++g) core += red2[g * DC + tid];
+        st_put_local(a.out + (size_t)h * D + c * DC + tid, f2bf(core));
       }
     }
     named_bar(1, ST_NT);
-    if (tid == 0)
-      for (int i = 0; i < ST_GDN_SLOTS; ++i) {  // a slot's empty barrier takes two arrivals
-        mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
-        mbar_arrive(X.empty0 + 8 * ((n + i) % ST_SLOTS));
-      }
-    n += ST_GDN_SLOTS;
+    if (tid == 0) {  // a slot's empty barrier takes two arrivals
+      mbar_arrive(X.empty0 + 8 * slot);
+      mbar_arrive(X.empty0 + 8 * slot);
+    }
+    ++n;
   }
 }
 

@@ -121,6 +121,23 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
       }
     }
     if (o.sl_in_count > 16) return cudaErrorInvalidValue;
+    // a PLAIN GEMV over the previous GatedDeltaNet stage's output applies
+    // that stage's gated RMSNorm in its prologue (whole heads of x)
+    o.gated_pro = 0;
+    if (in.pro == QWEN_STEP_PRO_PLAIN && !prev_in.empty() && prev_in.back().kind == QWEN_STEP_GDN &&
+        prev_in.back().g_z) {
+      const qwen_step_stage& g = prev_in.back();
+      const long long off = static_cast<const char*>(in.x) - static_cast<const char*>(g.g_out);
+      const long long head_bytes = (long long)g.g_dim * 2, span = (long long)g.g_heads * head_bytes;
+      if (off >= 0 && off < span) {
+        if (off % head_bytes || in.K % g.g_dim || off + 2LL * in.K > span || in.K > 4096 || in.wbf16)
+          return cudaErrorInvalidValue;
+        o.gated_pro = 1;
+        o.gz = static_cast<const bf16*>(g.g_z) + off / 2;
+        o.gnw = static_cast<const bf16*>(g.g_norm_w);
+        o.geps = g.g_eps;
+      }
+    }
     o.am_ws = in.am_ws;
     o.am_key_out = in.am_key_out;
     o.am_token_out = in.am_token_out;
@@ -133,6 +150,7 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
       switch (s.epi) {
         case QWEN_STEP_EPI_STORE:
         case QWEN_STEP_EPI_GATE_BETA:
+        case QWEN_STEP_EPI_SILU:
           if (!s.y) return cudaErrorInvalidValue;
           break;
         case QWEN_STEP_EPI_SILU_PAIR:
@@ -349,6 +367,10 @@ static int step_create_impl(const qwen_step_stage* stages, int nstages, int worl
     conv.push_back(o);
     ins.push_back(stages[i]);
   }
+  // a gated GatedDeltaNet stage leaves the gated RMSNorm to the GEMV after it
+  for (int i = 0; i < nstages; ++i)
+    if (stages[i].kind == QWEN_STEP_GDN && stages[i].g_z && (i + 1 >= nstages || !conv[i + 1].gated_pro))
+      return record(cudaErrorInvalidValue);
   const int* pos = nullptr;
   for (int i = 0; i < nstages; ++i)
     if (stages[i].kind == QWEN_STEP_ATTN) {

@@ -149,6 +149,10 @@ class Qwen35DecodeEngine:
         self.kernels_per_step = 0
 
     # ------------------------------------------------------------------
+    def gdn_state(self, i: int) -> torch.Tensor:
+        """Layer i's GatedDeltaNet state as [value heads][keys][values] FP32."""
+        return self.state[i]
+
     def reset(self):
         """Clear caches and recurrent state; position back to 0."""
         for t in list(self.k_cache.values()) + list(self.v_cache.values()):

@@ -8,7 +8,7 @@ walks (``include/qwen_step.h``):
     per layer (5 stages):
       full:   RMSNorm + q/k/v GEMVs | norm + RoPE + KV write + attention + gate | o_proj (K slices)
       linear: RMSNorm + in_proj GEMVs with conv1d/SiLU and gate epilogues
-              | delta rule + gated RMSNorm | out_proj (K slices)
+              | delta rule (units of 32 value columns) | gated RMSNorm + out_proj (K slices)
       both:   residual + RMSNorm + gate/up + SiLU | down (K slices)
     residual + RMSNorm + LM head + greedy argmax (+ position increment)
 
@@ -34,7 +34,7 @@ P = ctypes.c_void_p
 
 GEMV, GDN, ATTN = 0, 1, 2
 PRO_PLAIN, PRO_NORM, PRO_EMBED_NORM, PRO_SLICES_NORM = 0, 1, 2, 3
-EPI_STORE, EPI_SILU_PAIR, EPI_ARGMAX, EPI_CONV, EPI_GATE_G, EPI_GATE_BETA, EPI_SLICES = 0, 2, 3, 4, 5, 6, 9
+EPI_STORE, EPI_SILU_PAIR, EPI_ARGMAX, EPI_CONV, EPI_GATE_G, EPI_GATE_BETA, EPI_SLICES, EPI_SILU = 0, 2, 3, 4, 5, 6, 9, 10
 
 
 class StepSeg(ctypes.Structure):
@@ -144,6 +144,13 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
 
     def _create_program(self, stages):
         return create_program(stages)
+
+    def gdn_state(self, i: int) -> torch.Tensor:
+        """Layer i's GatedDeltaNet state as [value heads][keys][values] FP32 (a
+        copy: the step kernel keeps it as [heads][4 value blocks][keys][32])."""
+        st = self.state[i]
+        h, k, v = st.shape
+        return st.view(h, 4, k, v // 4).permute(0, 2, 1, 3).reshape(h, k, v)
 
     def _pack_all(self):
         w = self.w
@@ -264,7 +271,7 @@ class Qwen35StepEngine(Qwen35DecodeEngine):
             else:
                 segs = [self._seg(ly["in_proj_qkv"], EPI_CONV, y=self.qkv_conv, aux0=ly["conv1d_w"],
                                   aux2=self.conv_state[i], cw=cfg.linear_conv_kernel_dim),
-                        self._seg(ly["in_proj_z"], EPI_STORE, y=self.z),
+                        self._seg(ly["in_proj_z"], EPI_SILU, y=self.z),  # bf16(silu(z)) for the gated norm
                         self._seg(ly["in_proj_a"], EPI_GATE_G, y=self.g, aux0=ly["A_log"], aux1=ly["dt_bias"]),
                         self._seg(ly["in_proj_b"], EPI_GATE_BETA, y=self.beta)]
                 stages.append(self._gemv(H, segs=segs, **layer_input(i, ly)))

@@ -39,7 +39,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .step import (EPI_ARGMAX, EPI_CONV, EPI_GATE_BETA, EPI_GATE_G, EPI_SILU_PAIR, EPI_SLICES, EPI_STORE, P,
+from .step import (EPI_ARGMAX, EPI_CONV, EPI_GATE_BETA, EPI_GATE_G, EPI_SILU, EPI_SILU_PAIR, EPI_SLICES, EPI_STORE, P,
                    PRO_EMBED_NORM, PRO_PLAIN, PRO_SLICES_NORM, Qwen35StepEngine, StepStage)
 
 CHUNK_K, CHUNK_BYTES, TILE_ROWS = 512, 16400, 32
@@ -185,7 +185,7 @@ class Qwen35StepTPEngine(Qwen35StepEngine):
 
                 segs = [conv(hk0 * dk, hk1 * dk), conv(kd + hk0 * dk, kd + hk1 * dk),
                         conv(2 * kd + hv0 * dv, 2 * kd + hv1 * dv),
-                        self._sub(self._seg(ly["in_proj_z"], EPI_STORE, y=self.z), ly["in_proj_z"], hv0 * dv,
+                        self._sub(self._seg(ly["in_proj_z"], EPI_SILU, y=self.z), ly["in_proj_z"], hv0 * dv,
                                   hv1 * dv),
                         # the per-head gates (one row per value head) are computed whole on every rank
                         self._seg(ly["in_proj_a"], EPI_GATE_G, y=self.g, aux0=ly["A_log"], aux1=ly["dt_bias"]),

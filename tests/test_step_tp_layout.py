@@ -26,8 +26,8 @@ import pytest
 sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "qwen3.5-fp8-cuda_b200"))
 
 from qwen35_b200.config import qwen35_4b, qwen35_tiny  # noqa: E402
-from qwen35_b200.step import (ATTN, EPI_ARGMAX, EPI_CONV, EPI_GATE_BETA, EPI_GATE_G, EPI_SILU_PAIR,  # noqa: E402
-                              EPI_SLICES, EPI_STORE, GDN, GEMV, PRO_SLICES_NORM)
+from qwen35_b200.step import (ATTN, EPI_ARGMAX, EPI_CONV, EPI_GATE_BETA, EPI_GATE_G, EPI_SILU,  # noqa: E402
+                              EPI_SILU_PAIR, EPI_SLICES, EPI_STORE, GDN, GEMV, PRO_SLICES_NORM)
 from qwen35_b200.step_tp import CHUNK_BYTES, CHUNK_K, TILE_ROWS, Qwen35StepTPEngine  # noqa: E402
 
 WIN = 1 << 40
@@ -207,7 +207,7 @@ def test_tp_stage_split(cfg_name, world, bf16_head):
                         assert yoff == 4 * r0 and sp.where(sg.aux0)[1] == 4 * r0
                     elif sg.epi == EPI_ARGMAX:
                         assert sg.row_offset == r0 and (not sg.y or yoff == 2 * r0)
-                    elif sg.epi in (EPI_STORE, EPI_SILU_PAIR, EPI_GATE_BETA):
+                    elif sg.epi in (EPI_STORE, EPI_SILU_PAIR, EPI_GATE_BETA, EPI_SILU):
                         assert yoff == 2 * r0
                     cnt = rows.setdefault(mname, {})
                     for r in range(r0, r0 + sg.n):
