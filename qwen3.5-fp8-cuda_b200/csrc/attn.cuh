@@ -302,16 +302,18 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
   }
   if (nsplit == 1) return;
 
-  __threadfence();
+  // one acquire-release count per CTA: its release publishes the CTA's
+  // partials (ordered before it by the barrier), its acquire lets the last
+  // CTA's threads (ordered after it by the barrier) read every split's
   named_bar(1, NT);
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(a.ws_count + kh, 1u);
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.ws_count + kh) : "memory");
     s_last = prev == (unsigned)(nsplit - 1);
   }
   named_bar(1, NT);
   if (tl && threadIdx.x == 0) tl[1] = (unsigned)globaltimer_ns();
   if (!s_last) return;
-  __threadfence();
   const int n_active = (total + chunk - 1) / chunk;
   // Split weights f_s = exp(m_s - M) (held in the per-warp output area),
   // then every thread adds its (head, channel) pairs over the splits.
@@ -319,6 +321,23 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
   constexpr int FCAP = ATTN_WARPS * D;  // splits per head that fit
   const bool fits = n_active <= FCAP;
   if (fits) {
+    // every thread's (head, channel) pairs, added over the splits in split
+    // order below; the first SPI splits' partials and the output gates are
+    // loaded here, in the same round trip as the split weights
+    constexpr int PER = (G * D + NT - 1) / NT;
+    constexpr int SPI = PER <= 4 ? 8 : 4;  // splits per iteration: up to 32 loads in flight
+    float o[SPI][PER], gv[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int idx = threadIdx.x + k * NT;
+      gv[k] = (idx < G * D && a.gate) ? bf2f(__ldcg(a.gate + (size_t)(kh * G + idx / D) * a.q_stride + idx % D))
+                                      : 0.f;
+#pragma unroll
+      for (int j = 0; j < SPI; ++j)
+        o[j][k] = (idx < G * D && j < n_active)
+                      ? __ldcg(a.ws_part + ((size_t)(kh * G + idx / D) * nsplit + j) * (D + 2) + 2 + idx % D)
+                      : 0.f;
+    }
     // split weights: warp g, lanes over the splits; (M, L) of a split is one
     // 8-byte load, every lane's loads issued before the reductions
     constexpr int MAXL = 4;  // splits per lane held in registers (n_active <= 128)
@@ -357,30 +376,21 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, 
       if (lane == 0) wl[g] = L;
     }
     named_bar(1, NT);
-    // every thread adds its PER (head, channel) pairs over the splits in
-    // split order, four splits' loads of all its pairs in flight at a time
-    constexpr int PER = (G * D + NT - 1) / NT;
-    float Os[PER], gv[PER];
+    float Os[PER];
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      const int idx = threadIdx.x + k * NT;
-      Os[k] = 0.f;
-      gv[k] = 0.f;
-      if (idx < G * D && a.gate)
-        gv[k] = bf2f(__ldcg(a.gate + (size_t)(kh * G + idx / D) * a.q_stride + idx % D));
-    }
-    constexpr int SPI = PER <= 4 ? 8 : 4;  // splits per iteration: up to 32 loads in flight
+    for (int k = 0; k < PER; ++k) Os[k] = 0.f;
     for (int s = 0; s < n_active; s += SPI) {
-      float o[SPI][PER];
+      if (s > 0) {  // the next SPI splits (the first are loaded above)
 #pragma unroll
-      for (int j = 0; j < SPI; ++j)
+        for (int j = 0; j < SPI; ++j)
 #pragma unroll
-        for (int k = 0; k < PER; ++k) {
-          const int idx = threadIdx.x + k * NT;
-          o[j][k] = (idx < G * D && s + j < n_active)
-                        ? __ldcg(a.ws_part + ((size_t)(kh * G + idx / D) * nsplit + s + j) * (D + 2) + 2 + idx % D)
-                        : 0.f;
-        }
+          for (int k = 0; k < PER; ++k) {
+            const int idx = threadIdx.x + k * NT;
+            o[j][k] = (idx < G * D && s + j < n_active)
+                          ? __ldcg(a.ws_part + ((size_t)(kh * G + idx / D) * nsplit + s + j) * (D + 2) + 2 + idx % D)
+                          : 0.f;
+          }
+      }
 #pragma unroll
       for (int j = 0; j < SPI; ++j)
 #pragma unroll

@@ -1229,10 +1229,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     named_bar(1, ST_NT);
     if (tid == 0) {
       st_stamp(P, s, ST_TL_END);
-      if (s != P.drop_stage || blockIdx.x != 0) {
-        __threadfence();
-        atomicAdd(P.counters + P.nstages + s, 1ull);
-      }
+      if (s != P.drop_stage || blockIdx.x != 0)  // the release publishes what the CTA wrote (barrier-ordered)
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" :: "l"(P.counters + P.nstages + s) : "memory");
       prev_xrank = S.xrank;
     }
   }
