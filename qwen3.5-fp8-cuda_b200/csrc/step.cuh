@@ -375,7 +375,7 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
     if (S.kind == ST_GEMV) {
       // the stage's fields in registers: the copies below are asm with memory
       // clobbers, after which the compiler would reload them from global memory
-      const int ns = S.nslice, ipu = S.ipu, pair = S.pair, nseg = S.nseg;
+      const int ns = S.nslice, ipu = S.ipu, pair = S.pair, nseg = S.nseg, tiles_my = S.nunits / ns;
       const size_t tile_bytes = (size_t)S.cstride * ST_CHUNK, slice_bytes = (size_t)(S.C / ns) * ST_CHUNK;
       int t0[ST_MAX_SEG];
       const uint8_t* wa[ST_MAX_SEG];
@@ -389,7 +389,7 @@ __device__ __forceinline__ void st_producer(const StProgram& P, uint32_t ring, u
       st_range(S.nunits, u0, u1);
       const int shard0 = S.shard0;
       for (int u = u0; u < u1 && ok; ++u) {
-        const int tl = u / ns, sl = u - tl * ns, t = shard0 + tl;
+        const int sl = u / tiles_my, tl = u - sl * tiles_my, t = shard0 + tl;  // slice-major units
         const uint8_t* a = wa[0];
         const uint8_t* b = wb[0];
         int tb = t0[0];
@@ -504,9 +504,11 @@ __device__ __forceinline__ void st_ll_wait_all(const unsigned long long* sl, int
 
 template <int MB, int SLR, bool GATED = false>
 __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8_t* xl, float* xinv, float* red,
-                                            uint32_t ll_tag, unsigned* abort_flag) {
+                                            uint32_t ll_tag, unsigned* abort_flag, int blo, int bhi) {
+  // 128-wide blocks [blo, bhi) of x (a PLAIN prologue prepares only the K
+  // range of this CTA's units; a normalising one needs all of K)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int K = S.K, nb = K >> 7, pro = S.pro, nsl = S.sl_in_count, sl_stride = S.sl_stride;
+  const int K = S.K, nb = bhi, pro = S.pro, nsl = S.sl_in_count, sl_stride = S.sl_stride;
   // tagged slices of a row-parallel stage (tensor parallel): waited for
   // first, then read like FP32 slices (the low halves of the words)
   const bool ll = pro == STP_SLICES_NORM && S.sl_src >= 0;
@@ -535,7 +537,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   const int nreg = pro == STP_SLICES_NORM ? (nsl < SLR ? nsl : SLR) : 0;
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
-    const int b = warp + i * ST_CW;
+    const int b = blo + warp + i * ST_CW;
     const int k0 = b * 128 + lane * 4;
     if (b < nb) {
       raw[i] = pro == STP_EMBED_NORM ? __ldg(reinterpret_cast<const uint2*>(src + k0))
@@ -548,7 +550,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   if (ll) st_ll_wait_all(reinterpret_cast<const unsigned long long*>(sl_in), nsl, sl_stride, nb, ll_tag, abort_flag);
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
-    const int b = warp + i * ST_CW;
+    const int b = blo + warp + i * ST_CW;
     const int k0 = b * 128 + lane * 4;
     if (b < nb) {
 #pragma unroll
@@ -569,7 +571,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
     const float nw[4] = {w01.x, w01.y, w23.x, w23.y};
 #pragma unroll
     for (int i = 0; i < MB; ++i) {
-      const int b = warp + i * ST_CW;
+      const int b = blo + warp + i * ST_CW;
       const float cs = warp_sum(v[i][0] * v[i][0] + v[i][1] * v[i][1] + v[i][2] * v[i][2] + v[i][3] * v[i][3]);
       if (b >= nb) continue;  // warp-uniform
       const float inv = rsqrtf(cs / (float)ST_GDN_D + S.geps);
@@ -594,7 +596,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
     for (int c0 = nreg; c0 < nsl; c0 += SLR) {
 #pragma unroll
       for (int i = 0; i < MB; ++i) {
-        const int b = warp + i * ST_CW;
+        const int b = blo + warp + i * ST_CW;
 #pragma unroll
         for (int c = 0; c < SLR; ++c)
           if (b < nb && c0 + c < nsl)
@@ -616,7 +618,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
-    const int b = warp + i * ST_CW;
+    const int b = blo + warp + i * ST_CW;
     if (b >= nb) continue;
     const int k0 = b * 128 + lane * 4;
     if (h_out) {
@@ -660,7 +662,7 @@ __device__ __forceinline__ void st_prologue(const StStage& S, uint8_t* xh, uint8
     for (int i = 0; i < MB; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], o));
 #pragma unroll
   for (int i = 0; i < MB; ++i) {
-    const int b = warp + i * ST_CW;
+    const int b = blo + warp + i * ST_CW;
     if (b >= nb) continue;  // warp-uniform
     const int k0 = b * 128 + lane * 4;
     if (S.wbf16) {  // BF16 weights: x stays BF16 (xh holds K BF16 values)
@@ -917,14 +919,21 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int u0, u1;
   st_range(S.nunits, u0, u1);
-  if (S.pro == STP_PLAIN && S.gated_pro)
-    st_prologue<ST_GATED_MAXB, 0, true>(S, X.xh, X.xl, X.xinv, X.red, 0u, X.abort_flag);
-  else if (S.pro == STP_PLAIN)
-    st_prologue<ST_MAXB, 0>(S, X.xh, X.xl, X.xinv, X.red, 0u, X.abort_flag);
-  else
-    st_prologue<ST_NORM_MAXB, ST_SL_REG>(S, X.xh, X.xl, X.xinv, X.red, X.tag0 + (uint32_t)S.sl_src, X.abort_flag);
+  const int nslice = S.nslice, tiles_my = S.nunits / nslice;  // units are slice-major: u = sl x tiles_my + tile
+  if (S.pro == STP_PLAIN) {
+    // the K blocks of the slices this CTA's units cover
+    const int bps = (S.C / nslice) * (ST_KC / 128);
+    const int blo = u1 > u0 ? (u0 / tiles_my) * bps : 0, bhi = u1 > u0 ? ((u1 - 1) / tiles_my + 1) * bps : 0;
+    if (S.gated_pro)
+      st_prologue<ST_GATED_MAXB, 0, true>(S, X.xh, X.xl, X.xinv, X.red, 0u, X.abort_flag, blo, bhi);
+    else
+      st_prologue<ST_MAXB, 0>(S, X.xh, X.xl, X.xinv, X.red, 0u, X.abort_flag, blo, bhi);
+  } else {
+    st_prologue<ST_NORM_MAXB, ST_SL_REG>(S, X.xh, X.xl, X.xinv, X.red, X.tag0 + (uint32_t)S.sl_src, X.abort_flag,
+                                         0, S.K >> 7);
+  }
   if (tid == 0 && X.timeline) st_tl_put(X.timeline, X.stage, ST_TL_PRO, (unsigned)globaltimer_ns());
-  const int ipu = S.ipu, nslice = S.nslice, pair = S.pair;
+  const int ipu = S.ipu, pair = S.pair;
   const int upb = ST_BATCH / ipu > 0 ? ST_BATCH / ipu : 1;
   const int per = S.C / nslice;
   unsigned long long am_best = 0;
@@ -947,7 +956,7 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
         if (X.timeline) blocked += globaltimer_ns() - t0;
       }
       const int u = ub + q / ipu, i = q % ipu;
-      const int t = u / nslice, sl = u - t * nslice;
+      const int sl = u / tiles_my;
       const int c = sl * per + (pair ? (i >> 1) : i);
       float a0, a1;
       const long long tc = X.timeline ? clock64() : 0;
@@ -979,7 +988,7 @@ __device__ __forceinline__ void st_gemv(const StStage& S, const StCtx& X, uint32
       } else {
         for (int i = 0; i < ipu; ++i) v += pp[i * ST_ROWS];
       }
-      const int tl = u / nslice, sl = u - tl * nslice, t = S.shard0 + tl;
+      const int sl = u / tiles_my, tl = u - sl * tiles_my, t = S.shard0 + tl;
       const int sg = st_find_seg(S, t);
       const GemvSeg& G = S.seg[sg];
       const int row = (t - S.seg_tile0[sg]) * ST_ROWS + r;
