@@ -107,19 +107,10 @@ __device__ __forceinline__ void attn_prep_head(const bf16* src, const float* nor
 // the caller (else *a.pos_ptr).  U: positions per warp in flight; QREG:
 // the scaled queries held in registers (else re-read from shared memory per
 // position, for callers with a tighter register budget).
-// `peer_off` / `world` (tensor-parallel step kernel): the output is also
-// stored at out + peer_off[r] bytes for every rank r < world.
 template <int D, int G, int U = 4, bool QREG = true>
 __device__ __forceinline__ void attn_unit(const AttnArgs& a, int kh, int split, float* asmem, int* s_last_p,
-                                          unsigned* tl = nullptr, int pos_known = -1,
-                                          const long long* peer_off = nullptr, int world = 1) {
-  auto put_out = [&](size_t idx, bf16 ob) {
-    if (!peer_off || world == 1) {
-      a.out[idx] = ob;
-      return;
-    }
-    for (int r = 0; r < world; ++r) *reinterpret_cast<bf16*>(reinterpret_cast<char*>(a.out + idx) + peer_off[r]) = ob;
-  };
+                                          unsigned* tl = nullptr, int pos_known = -1) {
+  auto put_out = [&](size_t idx, bf16 ob) { a.out[idx] = ob; };
   constexpr int EPL = D / 32;
   constexpr int NT = ATTN_WARPS * 32;
   float* qsm = asmem;                       // [G][D] scaled query

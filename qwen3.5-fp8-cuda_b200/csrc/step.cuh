@@ -184,23 +184,21 @@ struct StProgram {
   const StStage* stages;
   int nstages;
   // [2 nstages + 1], monotonic over the program's steps (nothing is cleared):
-  // [0, nstages) stage completions, [nstages, 2 nstages) this rank's CTAs done
-  // with each stage (tensor parallel), [2 nstages] this rank's completed
-  // steps x grid, from which a launch takes its epoch e.  One GPU: stage s is
-  // complete when counters[s] (CTAs) reaches (e + 1) x grid.  Tensor
-  // parallel: a rank's CTAs count on its local counter; the last one adds 1
-  // to counters[s] of every rank (release, system scope), and stage s is
-  // complete when the local counters[s] reaches (e + 1) x world.  In the
-  // shared arena.
+  // [0, nstages) unused, [nstages, 2 nstages) this GPU's CTAs done with each
+  // stage, [2 nstages] this GPU's completed steps x grid, from which a launch
+  // takes its epoch e.  Stage s is complete on this GPU when
+  // counters[nstages + s] reaches (e + 1) x grid.  Tensor parallel: the
+  // stage after a row-parallel (xrank) stage polls that stage's tagged
+  // K-slice words of every rank instead (tag e x nstages + 1 + s).
   unsigned long long* counters;
   unsigned* abort_flag;  // set by a timed-out wait; every wait then gives up at once
   unsigned* timeline;    // optional [nstages][grid][ST_TL]: %globaltimer (low 32 bits, ns) per stage and CTA
   const int* pos;        // decode position read by the attention stages (constant within a step), or null
   int drop_stage;        // test hook: CTA 0 does not report stage drop_stage done (-1: off)
   // Tensor parallel (world > 1): rank r's copy of any shared-arena object is
-  // at the local address + peer_off[r] (peer_off[rank] = 0).  Stage outputs,
-  // K slices, counters, the argmax workspace, token, key and position live in
-  // the arena and are written to every rank.
+  // at the local address + peer_off[r] (peer_off[rank] = 0).  The tagged
+  // K-slice words of row-parallel stages, the LM-head logits and the argmax
+  // workspace are written to every rank; everything else stays local.
   int world, rank;
   long long peer_off[ST_MAX_WORLD];
 };

@@ -210,7 +210,7 @@ cudaError_t step_convert(const qwen_step_stage& in, qwen::StStage& o, int grid, 
     o.nslice = ns;
     o.nunits = my_tiles * ns;
     // tensor parallel: a row-parallel stage (this rank's K range, every row)
-    // writes its K-slice rows to every rank and is counted across the ranks
+    // writes its K-slice rows to every rank as tagged words
     o.xrank = (world > 1 && in.xrank) ? 1 : 0;
     if (o.xrank && (!slices || ns * world > 16)) return cudaErrorInvalidValue;
     o.cstride = in.cstride > 0 ? in.cstride : o.C;
