@@ -51,7 +51,11 @@ def run_head(lib, x, w, s, norm_w=None, row_offset=0, ws=None):
     return int(tok), int(key) & 0xFFFFFFFFFFFFFFFF, logits.cpu()
 
 
-def test_config2_token_bit_exact(lib, head):
+def test_config2_token_is_own_argmax_and_follows_oracle(lib, head):
+    """The fused token is exactly the first-index argmax of the kernel's own
+    BF16 logits (bit-exact check); against the oracle's FP32 logits the token
+    may differ only where the oracle's top two are a tie within rounding
+    (gap < 0.05), an explicit tolerance."""
     w, s = head
     wd, sd = w.cuda(), s.cuda()
     worst_gap = None
